@@ -1,0 +1,432 @@
+#!/usr/bin/env python3
+"""Benchmark of the L2-domain-aware B200 GEMV (one JSON line on rank 0).
+
+Workload (default ``cfg5``): the row-sharded fp16 GEMV of the configs -- A is M=131072 x N=16384
+fp16 (4 GiB), A ~ N(0, 0.02), x ~ N(0, 1), fp32 accumulation, fp16 y.  With N GPUs each rank owns
+M/N contiguous rows; one step is: NCCL broadcast of x from rank 0, the domain-aware GEMV of the
+rank's shard, NCCL all-gather of y.  With one GPU the step is the GEMV alone (the whole 4 GiB
+matrix).  Every rank's A is larger than L2 at every N <= 8 (>= 512 MiB), so no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg5]
+
+``--impl reference`` times the reference's CPU GEMV check loop (the oracle restatement of
+applications/gemv/src/gemv_k1024_persistent_subwarp.cu:383-390) on all host cores, over a bounded
+row sample of the same matrix, on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "GEMV GB/s (frac of HBM peak), µs/call; domain-aware vs naive, 1–8 B200"
+FALLBACK_HBM_GBS = 6650.0
+SPEC_HBM_GBS = 8000.0
+
+F32, F16, BF16 = 0, 1, 2
+UNIFORM, NORMAL = 0, 1
+DT_NAME = {F32: "fp32", F16: "fp16", BF16: "bf16"}
+EB = {F32: 4, F16: 2, BF16: 2}
+
+WORKLOADS = {
+    "cfg5": dict(M=131072, N=16384, batch=1, dtype=F16, a=(NORMAL, 0.0, 0.02), x=(NORMAL, 0.0, 1.0),
+                 name="row-sharded fp16 GEMV, A 131072x16384 (4 GiB), NCCL broadcast(x) + all_gather(y)"),
+    "cfg3": dict(M=28672, N=8192, batch=1, dtype=BF16, a=(NORMAL, 0.0, 0.02), x=(NORMAL, 0.0, 1.0),
+                 name="bf16 LLM-decode GEMV, A 28672x8192 (448 MiB)"),
+    "cfg4": dict(M=8192, N=8192, batch=32, dtype=F16, a=(UNIFORM, -0.05, 0.05), x=(NORMAL, 0.0, 1.0),
+                 name="batched fp16 GEMV, 32 x (8192x8192)"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg5")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline leg")
+    ap.add_argument("--no-aux", action="store_true", help="skip the per-mode and L2-resident side measurements")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy burst)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback (6.65 TB/s earlier pool measurement)"
+
+
+def profiled_traffic(workload: str, rows_local: int):
+    """DRAM bytes per launch from the committed ncu summary (profiles/), scaled to this launch."""
+    path = os.path.join(REPO, "profiles", f"gemv_{workload}_traffic.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_row:"):
+                    return float(line.split(":")[1]) * rows_local
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed region
+# ------------------------------------------------------------------------------------------------
+
+REASON_BITS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, torch_dev: int, period_s: float = 0.004):
+        self.samples, self.reasons, self.max_mhz, self.ok = [], 0, None, False
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            self.h = None
+            try:
+                import torch
+                p = torch.cuda.get_device_properties(torch_dev)
+                bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                self.h = N.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.h = N.nvmlDeviceGetHandleByIndex(torch_dev)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+            self._reasons_fn = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(N, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            self.ok = True
+        except Exception as e:  # noqa: BLE001 -- NVML is optional on the box
+            self.err = str(e)
+
+    def _sample(self):
+        N = self.N
+        self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
+        self.reasons |= int(self._reasons_fn(self.h))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._sample()
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+            self._sample()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        names = [n for b, n in REASON_BITS.items() if self.reasons & b]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------
+# Reference arm: the reference's CPU GEMV loop on all host cores
+# ------------------------------------------------------------------------------------------------
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    import oracle as O
+    W = WORKLOADS[args.workload]
+    N, dt = W["N"], W["dtype"]
+    rows = min(4096, W["M"])
+    A32 = O.cfg_fill(rows * N, 0, 0, *W["a"])
+    x32 = O.cfg_fill(N, 0, 1, *W["x"])
+    A = O.round_to(A32, dt)
+    x = O.round_to(x32, dt)
+    del A32, x32
+    cores = O.max_threads()
+    for _ in range(args.warmup):
+        O.gemv_threads(A, x, dt, rows, N, threads=cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.gemv_threads(A, x, dt, rows, N, threads=cores)
+    dt_s = (time.perf_counter() - t0) / max(args.steps, 1)
+    nbytes = rows * N * EB[dt] + N * EB[dt] + rows * EB[dt]
+    gbs = nbytes / dt_s / 1e9
+    sample = (f"rows 0..{rows - 1} of the {args.workload} matrix ({rows}x{N} {DT_NAME[dt]}, same generator and "
+              f"seed), sequential fp32 dot per row (gemv_k1024_persistent_subwarp.cu:383-390), rows split over "
+              f"{cores} threads")
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt_s * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": DT_NAME[dt], "data": "synthetic",
+        "config": {"workload": args.workload, "M": W["M"], "N": N, "batch": W["batch"], "sample_rows": rows},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# Our arm
+# ------------------------------------------------------------------------------------------------
+
+def cpu_baseline_leg(A_dev, x_dev, dt, N, budget_s):
+    """The oracle's single-threaded CPU check loop on the first rows of the same matrix."""
+    import torch
+
+    import oracle as O
+    rows = 1024
+    st = torch.int16 if dt != F32 else torch.float32
+    A = A_dev[: rows * N * EB[dt]].view(st).cpu().numpy()
+    x = x_dev[: N * EB[dt]].view(st).cpu().numpy()
+    if dt != F32:
+        A, x = A.view(np.uint16), x.view(np.uint16)
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        O.gemv_seq(A, x, dt, rows, N)
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    per = el / passes
+    nbytes = rows * N * EB[dt] + N * EB[dt] + rows * EB[dt]
+    return {"value": round(nbytes / per / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"rows 0..{rows - 1} ({rows}x{N} {DT_NAME[dt]}) of the same matrix, {passes} passes of the "
+                      f"sequential fp32 check loop (gemv_k1024_persistent_subwarp.cu:383-390), 1 thread, "
+                      f"{el:.1f} s"}
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import torch.distributed as dist
+
+    import l2domain_b200 as L
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    W = WORKLOADS[args.workload]
+    M, N, batch, dt = W["M"], W["N"], W["batch"], W["dtype"]
+    if batch != 1 and world > 1:
+        raise SystemExit("batched workloads run on one GPU")
+    if M % world:
+        raise SystemExit(f"M={M} does not split over {world} ranks")
+    m_loc = M // world
+    eb = EB[dt]
+    stream = torch.cuda.current_stream(dev)
+
+    # A shard: 2 MiB aligned, generated on the device (rows [rank*m_loc, (rank+1)*m_loc) of the matrix).
+    a_bytes = batch * m_loc * N * eb
+    raw = torch.empty(a_bytes + (2 << 20), dtype=torch.uint8, device=dev)
+    off = (-raw.data_ptr()) % (2 << 20)
+    A = raw[off: off + a_bytes]
+    L.fill_cfg(A, dt, batch * m_loc * N, 0, 0, *W["a"], first=rank * m_loc * N)
+    x = torch.empty(batch * N * eb, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        L.fill_cfg(x, dt, batch * N, 0, 1, *W["x"])
+    else:
+        x.zero_()
+    y_loc = torch.empty(batch * m_loc * eb, dtype=torch.uint8, device=dev)
+    y_full = torch.empty(batch * M * eb, dtype=torch.uint8, device=dev) if world > 1 else y_loc
+    torch.cuda.synchronize()
+
+    t_plan = time.perf_counter()
+    plan = L.GemvPlan(A, m_loc, N, dt, dt, batch=batch, device=local)
+    t_plan = time.perf_counter() - t_plan
+    pstats = plan.stats()
+
+    def step(mode=L.MODE_AWARE, ev=None):
+        if world > 1:
+            dist.broadcast(x, src=0)
+        if ev is not None:
+            ev[0].record(stream)
+        plan.gemv(A, x, y_loc, mode, stream)
+        if ev is not None:
+            ev[1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(y_full, y_loc)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # Sanity check against a float64 torch dot product on sampled rows (the oracle is not used here).
+    step()
+    torch.cuda.synchronize()
+    tdt = {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}[dt]
+    Av = A.view(tdt).view(batch * m_loc, N)
+    xv = x.view(tdt)
+    idx = torch.linspace(0, batch * m_loc - 1, 64, device=dev).long()
+    bidx = idx // m_loc
+    ref = (Av[idx].double() * xv.view(batch, N)[bidx].double()).sum(1)
+    got = y_loc.view(tdt)[idx].double()
+    rel = float(((got - ref).norm() / ref.norm()).item())
+    if not rel <= 2e-3:
+        raise SystemExit(f"rank {rank}: GEMV self-check failed, rel L2 {rel:.3g}")
+
+    # Headline: K timed steps of the aware GEMV (plus the collectives at N > 1).
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(L.MODE_AWARE, kev[i])
+        e1.record(stream)
+        e1.synchronize()
+    barrier()
+    step_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / args.steps)
+
+    bytes_loc = a_bytes + batch * N * eb + batch * m_loc * eb
+    total_bytes = bytes_loc * world
+    value = total_bytes / (step_ms * 1e-3) / 1e9
+    peak, peak_src = measured_peaks()
+    achieved = bytes_loc / (kern_ms * 1e-3) / 1e9
+    traffic = profiled_traffic(args.workload, batch * m_loc)
+
+    # Per-mode kernel times on the same data (the domain effect), and the cuBLAS comparator.
+    modes_us = {}
+    if not args.no_aux:
+        def kernel_time(fn, steps):
+            for _ in range(3):
+                fn()
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(steps):
+                fn()
+            b.record(stream)
+            b.synchronize()
+            return max_over_ranks(a.elapsed_time(b) / steps * 1e3)
+
+        for name, mode in (("aware", L.MODE_AWARE), ("oblivious", L.MODE_OBLIVIOUS), ("swapped", L.MODE_SWAPPED),
+                           ("stream", L.MODE_STREAM)):
+            modes_us[name] = round(kernel_time(lambda m=mode: plan.gemv(A, x, y_loc, m, stream), args.steps), 3)
+        if batch == 1:
+            out = torch.empty(m_loc, dtype=tdt, device=dev)
+            A2 = A.view(tdt).view(m_loc, N)
+            modes_us["cublas_torch_mv"] = round(kernel_time(lambda: torch.mv(A2, xv, out=out), args.steps), 3)
+        Ai = A.view(torch.int64)
+        modes_us["torch_sum_read"] = round(kernel_time(lambda: torch.sum(Ai), max(5, args.steps // 5)), 3)
+
+    # End to end through the public API: pinned x in, y out, every step.
+    x_host = torch.empty_like(x, device="cpu").pin_memory()
+    x_host.copy_(x)
+    y_host = torch.empty_like(y_full, device="cpu").pin_memory()
+
+    def e2e_step():
+        if rank == 0:
+            x.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y_full, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b.record(stream)
+    b.synchronize()
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / args.steps)
+    barrier()
+    fstats = plan.stats()
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline_leg(A, x, dt, N, args.cpu_seconds)
+
+    if rank == 0:
+        clocks = sampler.summary()
+        ratio = None
+        if modes_us.get("oblivious") and modes_us.get("aware"):
+            ratio = round(modes_us["oblivious"] / modes_us["aware"], 4)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_ms, 6), "us_per_call": round(step_ms * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": DT_NAME[dt],
+            "data": "synthetic: seeded splitmix64 stream, A~N(0,0.02), x~N(0,1) (cfg5 distributions), generated on device",
+            "config": {"workload": f"{args.workload}: {W['name']}", "M": M, "N": N, "batch": batch,
+                       "dtype_in": DT_NAME[dt], "dtype_out": DT_NAME[dt], "rows_per_gpu": m_loc,
+                       "parallelism": f"row-shard x{world}" + (", NCCL broadcast(x) + all_gather(y)" if world > 1 else ""),
+                       "mode": "aware", "l2": f"inputs larger than L2 ({a_bytes / 2**20:.0f} MiB of A per GPU), no flush"},
+            "modes_us": modes_us, "aware_speedup_vs_oblivious": ratio,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src,
+                         "frac_of_spec_8TBs": round(achieved / SPEC_HBM_GBS, 4), "kernel_us": round(kern_ms * 1e3, 3),
+                         "bytes_per_launch": bytes_loc},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(x.numel()), "d2h_bytes_per_step": int(y_full.numel()),
+                    "ms_per_step": round(e2e_ms, 6)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "plan": {"probe_and_plan_s": round(t_plan, 3), "domain_sms": pstats["domain_sms"],
+                     "granule_shift": pstats["granule_shift"], "domain_bytes": pstats["domain_bytes"],
+                     "split_rows": pstats["split_rows"], "fallback_slots": fstats["fallback_slots"],
+                     "calls": fstats["calls"]},
+            "check": {"rows": 64, "rel_l2_vs_f64": rel},
+        }
+        print(json.dumps(line), flush=True)
+    plan.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.gpus != world and world != 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,222 @@
+/*
+ * l2d.h -- C ABI of libl2d, the B200-native L2-domain-aware GEMV (y = A.x).
+ *
+ * All entry points are `extern "C"`, take plain pointers and sizes, return an int status
+ * (L2D_OK = 0, negative on error) and never abort the process.  The message of the last
+ * failure on the calling thread is available from l2d_last_error().
+ *
+ * Device work is stream-ordered on the caller's cudaStream_t (passed as void*; NULL = the
+ * legacy default stream).  A plan belongs to one device and must not be used concurrently
+ * from several threads without external locking.
+ *
+ * Reference interfaces replaced (LyleLuo/L2Domain; paths relative to that project):
+ *   l2d_probe_sm_domains    utility/latopt.cuh:532 get_map_smid2side<T>(T*, size_t&) and the
+ *                           standalone tool utility/get_smid2side.cu:114-189
+ *   l2d_probe_addr_domains  utility/latopt.cuh:784 get_map_memory_attr<T>(...) and the
+ *                           standalone tool utility/get_mask.cu:172-267
+ *   l2d_predict_far         utility/latopt.cuh:255-263 predict_map_memory_attr_far
+ *   l2d_predict_addr_side   applications/gemv/src/gemv_k1024_persistent_subwarp.cu:105-108
+ *   l2d_partition_rows      applications/gemv/src/gemv_k1024_persistent_subwarp.cu:261-273
+ *   l2d_plan_create         applications/gemv/src/gemv_k1024_persistent_subwarp.cu:73-103 (build_side_info)
+ *   l2d_gemv                applications/gemv/src/gemv_k1024_persistent_subwarp.cu:163-231
+ *                           (gemv_partitioned_kernel / gemv_baseline_kernel launches, :301-334)
+ *   l2d_l2_flush            utility/latopt.cuh:103-134,190 (GlobalL2Cache::reset)
+ *   l2d_fill_*              applications/gemv/src/gemv_k1024_persistent_subwarp.cu:118-139 (init_data)
+ *   l2d_write_smid2side_csv / l2d_read_smid2side_csv   utility/get_smid2side.cu:163-177 file format
+ *   l2d_write_mask_csv / l2d_read_mask_csv             utility/get_mask.cu:242-252 file format
+ */
+#ifndef L2D_H
+#define L2D_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define L2D_API __attribute__((visibility("default")))
+#else
+#define L2D_API
+#endif
+
+#define L2D_VERSION 100
+
+/* ---- status codes ---- */
+enum {
+    L2D_OK = 0,
+    L2D_ERR_INVALID = -1,          /* bad argument or unsupported shape */
+    L2D_ERR_CUDA = -2,             /* CUDA runtime error */
+    L2D_ERR_NO_DEVICE = -3,        /* no usable CUDA device */
+    L2D_ERR_PROBE_TIMEOUT = -4,    /* a bounded device-side wait ran out */
+    L2D_ERR_PROBE_COVERAGE = -5,   /* the probe did not see exactly one CTA per SM */
+    L2D_ERR_PROBE_AMBIGUOUS = -6,  /* latencies do not separate into a near and a far class */
+    L2D_ERR_UNSUPPORTED = -7,
+    L2D_ERR_IO = -8,               /* file read/write or format error */
+    L2D_ERR_NCCL = -9,
+    L2D_ERR_NOT_LINEAR = -10       /* the address hash is not XOR-linear within a 2 MiB page */
+};
+
+/* ---- element types and execution modes ---- */
+enum { L2D_F32 = 0, L2D_F16 = 1, L2D_BF16 = 2 };
+enum {
+    L2D_MODE_OBLIVIOUS = 0, /* domain-oblivious control: same kernel, pseudo-random granule split */
+    L2D_MODE_AWARE = 1,     /* every SM streams only granules homed in its own L2 domain */
+    L2D_MODE_SWAPPED = 2,   /* negative control: every SM streams only far-domain granules */
+    L2D_MODE_STREAM = 3     /* plain streaming GEMV, no split (whole rows per warp) */
+};
+
+L2D_API int l2d_version(void);
+L2D_API const char *l2d_last_error(void);
+L2D_API const char *l2d_status_string(int status);
+
+/* ---- domain probes ---- */
+typedef struct {
+    uint32_t timeout_ms;      /* bound of every device-side wait (0 = 1000 ms) */
+    uint32_t lines_per_sm;    /* probe lines per SM for the SM map (0 = 48) */
+    uint32_t lines_per_page;  /* attr votes per 2 MiB page (0 = 5) */
+    uint32_t mask_pages;      /* pages used to fit the mask (0 = 4) */
+    uint32_t reserved[4];
+} l2d_probe_opts;
+
+enum { L2D_BEHAVIOR_UNKNOWN = 0, L2D_BEHAVIOR_HOME_ONLY = 1, L2D_BEHAVIOR_NEAR_COPY = 2 };
+
+typedef struct {
+    int num_sm;              /* SMs seen (one CTA each) */
+    int leader_smid;         /* SM that primed the lines */
+    int behavior;            /* L2D_BEHAVIOR_*: whether an L2 half keeps copies of far lines */
+    int domain_sms[2];       /* SMs per domain (domain 0 = the domain of SM 0) */
+    float near_cycles;       /* mean latency of the near class */
+    float far_cycles;        /* mean latency of the far class */
+    float threshold;         /* 2-means split point */
+    float separation;        /* (far - near) / pooled standard deviation */
+    float min_agreement;     /* worst per-SM vote agreement in [0, 1] */
+    uint32_t device_status;  /* device status bits (timeouts) */
+    double elapsed_ms;       /* wall time of the probe kernel */
+} l2d_sm_probe_report;
+
+typedef struct {
+    uint32_t mask;           /* within-page hash bits */
+    int granule_shift;       /* log2 of the smallest domain-uniform block (lowest mask bit, 21 if mask = 0) */
+    float near_cycles, far_cycles, threshold, separation;
+    float mask_agreement;    /* share of random validation lines the linear model predicts */
+    float attr_agreement;    /* worst per-page vote agreement */
+    double domain1_fraction; /* share of the region's granules homed in domain 1 */
+    uint32_t device_status;
+    double elapsed_ms;
+} l2d_addr_probe_report;
+
+/* SM -> L2 domain map (replaces latopt.cuh:532).  map[smid] in {0, 1}; domain 0 is SM 0's.
+ * `cap` entries are available in map; *num_sm receives the SM count.  map == NULL only queries
+ * *num_sm.  report and raw are optional; raw receives, when raw_cap allows, the CTA->smid list
+ * followed by the target-first, target-second and leader latency matrices (uint32 cycles). */
+L2D_API int l2d_probe_sm_domains(int device, int *map, int cap, int *num_sm, const l2d_probe_opts *opts);
+L2D_API int l2d_probe_sm_domains_ex(int device, int *map, int cap, int *num_sm, const l2d_probe_opts *opts,
+                                    l2d_sm_probe_report *report, uint32_t *raw, size_t raw_cap, size_t *raw_len);
+
+/* Address -> L2 domain model of the region [base, base+bytes) (replaces latopt.cuh:784).
+ * base must be 2 MiB aligned.  attr receives one entry per 2 MiB page (cap_pages entries);
+ * *num_pages receives the page count.  attr == NULL only queries *num_pages. */
+L2D_API int l2d_probe_addr_domains(int device, const void *base, size_t bytes, const int *sm_map, int num_sm,
+                                   uint32_t *mask, int *attr, size_t cap_pages, size_t *num_pages,
+                                   const l2d_probe_opts *opts);
+L2D_API int l2d_probe_addr_domains_ex(int device, const void *base, size_t bytes, const int *sm_map, int num_sm,
+                                      uint32_t *mask, int *attr, size_t cap_pages, size_t *num_pages,
+                                      const l2d_probe_opts *opts, l2d_addr_probe_report *report, uint32_t *raw,
+                                      size_t raw_cap, size_t *raw_len);
+
+/* Host-side analysis used by the probes, exported so it can be tested without a GPU.
+ * l2d_analyze_sm: lat_* are [n_cta x lines] matrices; smid_of_cta[n_cta]; writes map[smid]. */
+L2D_API int l2d_analyze_sm(int n_cta, int lines, const uint32_t *smid_of_cta, const uint32_t *lat_target,
+                           const uint32_t *lat_leader, int *map, int map_cap, l2d_sm_probe_report *report);
+/* l2d_analyze_addr: offsets[n] (bytes from base), lat[n] measured from domain 0, kind[n]:
+ * 0 = mask-fit line of page page_of[n] (offset 0 and 2^b), 1 = validation line, 2 = attr vote. */
+L2D_API int l2d_analyze_addr(size_t n, const uint64_t *offsets, const uint32_t *lat, const uint8_t *kind,
+                             size_t num_pages, uint32_t *mask, int *attr, l2d_addr_probe_report *report);
+/* 2-means split of a latency sample; returns L2D_ERR_PROBE_AMBIGUOUS when the classes overlap. */
+L2D_API int l2d_kmeans2(const uint32_t *lat, size_t n, float *threshold, float *near_mean, float *far_mean,
+                        float *separation);
+
+/* ---- predictor and placement (host) ---- */
+L2D_API int l2d_predict_far(int side, uint32_t mask, uint64_t addr, int attr);
+L2D_API int l2d_predict_addr_side(uint64_t base, uint32_t mask, const int *attr, size_t n_attr, uint64_t addr);
+L2D_API int l2d_partition_rows(uint64_t base, uint64_t row_bytes, int64_t M, uint32_t mask, const int *attr,
+                               size_t n_attr, int32_t *side0, int64_t *n0, int32_t *side1, int64_t *n1,
+                               int32_t *base0, int64_t *nb0, int32_t *base1, int64_t *nb1);
+
+/* ---- calibration files in the reference formats ---- */
+L2D_API int l2d_write_smid2side_csv(const char *path, const int *map, int num_sm);
+L2D_API int l2d_read_smid2side_csv(const char *path, int *map, int cap, int *num_sm);
+L2D_API int l2d_write_mask_csv(const char *path, uint32_t mask);
+L2D_API int l2d_read_mask_csv(const char *path, uint32_t *mask);
+
+/* ---- GEMV plans ---- */
+typedef struct l2d_plan l2d_plan;
+
+typedef struct {
+    int64_t M;          /* rows per problem */
+    int64_t N;          /* columns (the reference's K) */
+    int64_t lda;        /* elements between rows (>= N; 0 = N) */
+    int dtype_in;       /* A and x storage: L2D_F32 / L2D_F16 / L2D_BF16 */
+    int dtype_out;      /* y storage */
+    int64_t batch;      /* independent problems (0 or 1 = single) */
+    int64_t stride_a;   /* elements between consecutive problems' A (0 = M*lda) */
+    int64_t stride_x;   /* elements between consecutive x (0 = N) */
+    int64_t stride_y;   /* elements between consecutive y (0 = M) */
+    int device;
+    const void *A;      /* the A allocation the plan's domain map describes */
+    int flags;          /* L2D_PLAN_* */
+} l2d_gemv_desc;
+
+enum { L2D_PLAN_NO_PROBE = 1 /* skip the domain probes: only L2D_MODE_STREAM is available */ };
+
+typedef struct {
+    int num_sm;
+    const int *sm_domain;   /* [num_sm] */
+    uint32_t mask;
+    const int *attr;        /* [num_pages] per 2 MiB page of the region starting at base */
+    size_t num_pages;
+    const void *base;       /* 2 MiB aligned; must cover every row of A */
+} l2d_domain_map;
+
+typedef struct {
+    int64_t rows_total;          /* batch * M */
+    int granule_shift;
+    int64_t domain_bytes[2];     /* A bytes homed in each domain */
+    int64_t split_rows;          /* rows with granules in both domains */
+    int domain_sms[2];
+    int grid, block;
+    size_t scratch_bytes;        /* device scratch the plan owns */
+    uint64_t fallback_slots;     /* slots processed away from their home SM so far */
+    uint64_t calls;              /* completed kernel calls (device epoch) */
+} l2d_plan_stats;
+
+/* Creates a plan.  map == NULL probes the device and desc->A's region (2 MiB pages covering
+ * every row).  The plan owns its device scratch (allocated here, never during l2d_gemv). */
+L2D_API int l2d_plan_create(const l2d_gemv_desc *desc, const l2d_domain_map *map, l2d_plan **plan);
+L2D_API int l2d_plan_destroy(l2d_plan *plan);
+/* y = A.x for every problem, stream-ordered; A must be desc->A (the planned allocation). */
+L2D_API int l2d_gemv(l2d_plan *plan, const void *A, const void *x, void *y, int mode, void *stream);
+/* Synchronises the device and reads the plan's device counters into *stats. */
+L2D_API int l2d_plan_stats_get(l2d_plan *plan, l2d_plan_stats *stats);
+/* The plan's SM->domain map and mask/attr (for the CLI and the calibration files). */
+L2D_API int l2d_plan_domain_map(const l2d_plan *plan, int *sm_domain, int cap, int *num_sm, uint32_t *mask);
+
+/* ---- helpers used by the benchmark and the CLI ---- */
+/* Reference-mode inputs (init_data): A/x from mix32 of the flat index (stream 0 = A, 1 = x). */
+L2D_API int l2d_fill_ref(void *dst, int dtype, uint64_t first, uint64_t n, uint32_t seed, int stream,
+                         int integer_mode, void *stream_handle);
+/* BASELINE-config inputs: dist 0 uniform[p0,p1], 1 normal(mean p0, sigma p1), rounded to dtype. */
+L2D_API int l2d_fill_cfg(void *dst, int dtype, uint64_t first, uint64_t n, uint64_t seed, uint64_t rng_stream,
+                         int dist, float p0, float p1, void *stream_handle);
+/* Evicts the L2 by writing a device buffer of the L2's size (GlobalL2Cache::reset). */
+L2D_API int l2d_l2_flush(int device, void *stream_handle);
+/* Device properties the roofline needs. */
+L2D_API int l2d_device_info(int device, int *num_sm, int *l2_bytes, int *cc_major, int *cc_minor, char *name,
+                            int name_cap);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* L2D_H */

@@ -1,0 +1,245 @@
+// Input generators, the L2 flush and device information.
+//
+// l2d_fill_ref restates init_data (applications/gemv/src/gemv_k1024_persistent_subwarp.cu:118-139):
+// A[i] = (mix32(uint32(i) ^ seed) & 0xff) / 255 - 0.5 (x uses seed + 0x9e37), or the exact-integer
+// mode of :122-134.  l2d_fill_cfg draws the BASELINE distributions from a counter-based
+// splitmix64 stream; the normal draw is Box-Muller with a textbook log series and a Taylor cosine,
+// every operation written with explicit round-to-nearest intrinsics so the host generator
+// computes identical values.  Storage rounding is IEEE round-to-nearest-even.
+#include "l2d_internal.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <map>
+#include <mutex>
+
+namespace l2d {
+namespace gen {
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z) {
+    z += 0x9e3779b97f4a7c15ull;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ double dfma_free(double p, double s2, double c) { return __dadd_rn(__dmul_rn(p, s2), c); }
+
+__device__ double log_pos(double u) {
+    uint64_t bits = static_cast<uint64_t>(__double_as_longlong(u));
+    int e = static_cast<int>((bits >> 52) & 0x7ff) - 1023;
+    uint64_t mbits = (bits & 0x000fffffffffffffull) | 0x3ff0000000000000ull;
+    double m = __longlong_as_double(static_cast<long long>(mbits));
+    if (m > 1.4142135623730951) {
+        m = __dmul_rn(m, 0.5);
+        e = e + 1;
+    }
+    double s = __ddiv_rn(__dsub_rn(m, 1.0), __dadd_rn(m, 1.0));
+    double s2 = __dmul_rn(s, s);
+    double p = 1.0 / 23.0;
+    p = dfma_free(p, s2, 1.0 / 21.0);
+    p = dfma_free(p, s2, 1.0 / 19.0);
+    p = dfma_free(p, s2, 1.0 / 17.0);
+    p = dfma_free(p, s2, 1.0 / 15.0);
+    p = dfma_free(p, s2, 1.0 / 13.0);
+    p = dfma_free(p, s2, 1.0 / 11.0);
+    p = dfma_free(p, s2, 1.0 / 9.0);
+    p = dfma_free(p, s2, 1.0 / 7.0);
+    p = dfma_free(p, s2, 1.0 / 5.0);
+    p = dfma_free(p, s2, 1.0 / 3.0);
+    p = dfma_free(p, s2, 1.0);
+    double lm = __dmul_rn(__dmul_rn(2.0, s), p);
+    return __dadd_rn(__dmul_rn(static_cast<double>(e), 0.6931471805599453), lm);
+}
+
+// sum_k (-1)^k x^(2k) / (2k)!, k = 0..9, Horner in x^2.
+__device__ double cos_series(double x) {
+    double x2 = __dmul_rn(x, x);
+    double p = -1.0 / 6402373705728000.0;
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 20922789888000.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 87178291200.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 479001600.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 3628800.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 40320.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 720.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 24.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 0.5);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0);
+    return p;
+}
+
+// x * sum_k (-1)^k x^(2k) / (2k+1)!, k = 0..9.
+__device__ double sin_series(double x) {
+    double x2 = __dmul_rn(x, x);
+    double p = -1.0 / 121645100408832000.0;
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 355687428096000.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 1307674368000.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 6227020800.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 39916800.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 362880.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 5040.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0 / 120.0);
+    p = __dsub_rn(__dmul_rn(p, x2), 1.0 / 6.0);
+    p = __dadd_rn(__dmul_rn(p, x2), 1.0);
+    return __dmul_rn(p, x);
+}
+
+__device__ double cos_2pi(double u) {
+    double w = __dsub_rn(u, 0.5);
+    double sign = -1.0;
+    if (w < 0.0) w = -w;
+    if (w > 0.25) {
+        w = __dsub_rn(0.5, w);
+        sign = -sign;
+    }
+    if (w > 0.125) return __dmul_rn(sign, sin_series(__dmul_rn(__dsub_rn(0.25, w), 6.283185307179586)));
+    return __dmul_rn(sign, cos_series(__dmul_rn(w, 6.283185307179586)));
+}
+
+__device__ __forceinline__ uint64_t rng_u64(uint64_t seed, uint64_t stream, uint64_t index, uint32_t sub) {
+    uint64_t key = splitmix64(seed ^ (stream * 0xd1342543de82ef95ull) ^ 0x243f6a8885a308d3ull);
+    return splitmix64(key + 2ull * index + sub);
+}
+
+__device__ float cfg_value(uint64_t seed, uint64_t stream, uint64_t index, int dist, float p0, float p1) {
+    uint64_t r0 = rng_u64(seed, stream, index, 0);
+    if (dist == 0) {
+        float u = __fmul_rn(__uint2float_rn(static_cast<uint32_t>(r0 >> 40)), 0x1p-24f);
+        float span = __fsub_rn(p1, p0);
+        return __fadd_rn(p0, __fmul_rn(span, u));
+    }
+    uint64_t r1 = rng_u64(seed, stream, index, 1);
+    double u1 = __dmul_rn(__ull2double_rn((r0 >> 11) + 1ull), 0x1p-53);
+    double u2 = __dmul_rn(__ull2double_rn(r1 >> 11), 0x1p-53);
+    double l = log_pos(u1);
+    double r = __dsqrt_rn(__dmul_rn(-2.0, l));
+    double z = __dmul_rn(r, cos_2pi(u2));
+    double v = __dadd_rn(__dmul_rn(static_cast<double>(p1), z), static_cast<double>(p0));
+    return __double2float_rn(v);
+}
+
+__device__ __forceinline__ void store(void *dst, int dtype, uint64_t j, float v) {
+    if (dtype == L2D_F32) static_cast<float *>(dst)[j] = v;
+    else if (dtype == L2D_F16) static_cast<__half *>(dst)[j] = __float2half_rn(v);
+    else static_cast<__nv_bfloat16 *>(dst)[j] = __float2bfloat16_rn(v);
+}
+
+__global__ void k_fill_ref(void *dst, int dtype, uint64_t first, uint64_t n, uint32_t seed, int stream, int integer) {
+    const uint32_t s = stream == 0 ? seed : seed + 0x9e37u;
+    for (uint64_t j = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; j < n;
+         j += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        uint32_t h = mix32(static_cast<uint32_t>(first + j) ^ s);
+        float v;
+        if (integer) v = stream == 0 ? static_cast<float>(static_cast<int>(h % 17u) - 8)
+                                     : static_cast<float>(static_cast<int>(h % 7u) - 3);
+        else v = __fsub_rn(__fdiv_rn(__uint2float_rn(h & 0xffu), 255.0f), 0.5f);
+        store(dst, dtype, j, v);
+    }
+}
+
+__global__ void k_fill_cfg(void *dst, int dtype, uint64_t first, uint64_t n, uint64_t seed, uint64_t rs, int dist,
+                           float p0, float p1) {
+    for (uint64_t j = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; j < n;
+         j += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        store(dst, dtype, j, cfg_value(seed, rs, first + j, dist, p0, p1));
+}
+
+int fill_grid(uint64_t n) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    uint64_t want = (n + 255) / 256;
+    uint64_t cap = static_cast<uint64_t>(sms) * 16;
+    return static_cast<int>(want < cap ? (want ? want : 1) : cap);
+}
+
+std::mutex g_flush_mu;
+std::map<int, std::pair<void *, size_t>> g_flush;  // device -> flush buffer (kept until exit)
+
+}  // namespace gen
+}  // namespace l2d
+
+using namespace l2d;
+
+extern "C" {
+
+int l2d_fill_ref(void *dst, int dtype, uint64_t first, uint64_t n, uint32_t seed, int stream, int integer_mode,
+                 void *stream_handle) {
+    clear_error();
+    if (!valid_dtype(dtype)) return set_error(L2D_ERR_INVALID, "bad dtype");
+    if (n == 0) return L2D_OK;
+    if (!dst) return set_error(L2D_ERR_INVALID, "null destination");
+    gen::k_fill_ref<<<gen::fill_grid(n), 256, 0, static_cast<cudaStream_t>(stream_handle)>>>(dst, dtype, first, n,
+                                                                                           seed, stream, integer_mode);
+    L2D_CUDA_TRY(cudaGetLastError());
+    return L2D_OK;
+}
+
+int l2d_fill_cfg(void *dst, int dtype, uint64_t first, uint64_t n, uint64_t seed, uint64_t rng_stream, int dist,
+                 float p0, float p1, void *stream_handle) {
+    clear_error();
+    if (!valid_dtype(dtype) || (dist != 0 && dist != 1)) return set_error(L2D_ERR_INVALID, "bad dtype or dist");
+    if (n == 0) return L2D_OK;
+    if (!dst) return set_error(L2D_ERR_INVALID, "null destination");
+    gen::k_fill_cfg<<<gen::fill_grid(n), 256, 0, static_cast<cudaStream_t>(stream_handle)>>>(dst, dtype, first, n,
+                                                                                           seed, rng_stream, dist, p0, p1);
+    L2D_CUDA_TRY(cudaGetLastError());
+    return L2D_OK;
+}
+
+int l2d_l2_flush(int device, void *stream_handle) {
+    clear_error();
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != device) L2D_CUDA_TRY(cudaSetDevice(device));
+    std::pair<void *, size_t> buf{nullptr, 0};
+    {
+        std::lock_guard<std::mutex> lk(gen::g_flush_mu);
+        auto it = gen::g_flush.find(device);
+        if (it == gen::g_flush.end()) {
+            int l2 = 0;
+            L2D_CUDA_TRY(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, device));
+            size_t bytes = static_cast<size_t>(l2) * 2;  // both L2 halves, with margin
+            void *p = nullptr;
+            L2D_CUDA_TRY(cudaMalloc(&p, bytes));
+            it = gen::g_flush.emplace(device, std::make_pair(p, bytes)).first;
+        }
+        buf = it->second;
+    }
+    cudaError_t e = cudaMemsetAsync(buf.first, 0, buf.second, static_cast<cudaStream_t>(stream_handle));
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "l2_flush: %s", cudaGetErrorString(e));
+    return L2D_OK;
+}
+
+int l2d_device_info(int device, int *num_sm, int *l2_bytes, int *cc_major, int *cc_minor, char *name, int name_cap) {
+    clear_error();
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return set_error(L2D_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= ndev) return set_error(L2D_ERR_INVALID, "device %d out of range", device);
+    cudaDeviceProp prop;
+    L2D_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (num_sm) *num_sm = prop.multiProcessorCount;
+    if (l2_bytes) *l2_bytes = prop.l2CacheSize;
+    if (cc_major) *cc_major = prop.major;
+    if (cc_minor) *cc_minor = prop.minor;
+    if (name && name_cap > 0) {
+        std::strncpy(name, prop.name, static_cast<size_t>(name_cap) - 1);
+        name[name_cap - 1] = '\0';
+    }
+    return L2D_OK;
+}
+
+}  // extern "C"
