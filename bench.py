@@ -265,16 +265,20 @@ def run_ours(args, rank, world, local):
     t_plan = time.perf_counter() - t_plan
     pstats = plan.stats()
 
+    from l2domain_b200.shard import RowShard, ShardedGemvStep
+
+    shard = RowShard(M, world, rank)
+    assert shard.rows == m_loc and shard.row0 == rank * m_loc
+
     def step(mode=L.MODE_AWARE, ev=None):
-        if world > 1:
-            dist.broadcast(x, src=0)
-        if ev is not None:
-            ev[0].record(stream)
-        plan.gemv(A, x, y_loc, mode, stream)
-        if ev is not None:
-            ev[1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(y_full, y_loc)
+        def local():
+            if ev is not None:
+                ev[0].record(stream)
+            plan.gemv(A, x, y_loc, mode, stream)
+            if ev is not None:
+                ev[1].record(stream)
+
+        ShardedGemvStep(shard, x, y_loc, y_full, local)()
 
     def barrier():
         if world > 1:
@@ -351,6 +355,49 @@ def run_ours(args, rank, world, local):
         Ai = A.view(torch.int64)
         modes_us["torch_sum_read"] = round(kernel_time(lambda: torch.sum(Ai), max(5, args.steps // 5)), 3)
 
+    # Side measurement, not the headline: config 2, the L2-resident fp16 4096x4096 GEMV (32 MiB),
+    # 1000 back-to-back calls per mode without a flush, where the near/far L2 latency shows.
+    l2res = None
+    if not args.no_aux and world == 1:
+        m2, n2 = 4096, 4096
+        raw2 = torch.empty(m2 * n2 * 2 + (2 << 20), dtype=torch.uint8, device=dev)
+        o2 = (-raw2.data_ptr()) % (2 << 20)
+        A2b = raw2[o2: o2 + m2 * n2 * 2]
+        L.fill_cfg(A2b, F16, m2 * n2, 0, 0, NORMAL, 0.0, 0.02)
+        x2 = torch.empty(n2 * 2, dtype=torch.uint8, device=dev)
+        L.fill_cfg(x2, F16, n2, 0, 1, NORMAL, 0.0, 1.0)
+        y2 = torch.empty(m2 * 2, dtype=torch.uint8, device=dev)
+        plan2 = L.GemvPlan(A2b, m2, n2, F16, F16, device=local)
+        l2res = {"workload": "cfg2: fp16 4096x4096 (32 MiB, L2-resident), 1000 back-to-back calls, no flush"}
+        for name, mode in (("aware", L.MODE_AWARE), ("oblivious", L.MODE_OBLIVIOUS), ("swapped", L.MODE_SWAPPED),
+                           ("stream", L.MODE_STREAM)):
+            for _ in range(20):
+                plan2.gemv(A2b, x2, y2, mode, stream)
+            torch.cuda.synchronize()
+            a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a2.record(stream)
+            for _ in range(1000):
+                plan2.gemv(A2b, x2, y2, mode, stream)
+            b2.record(stream)
+            b2.synchronize()
+            l2res[f"{name}_us"] = round(a2.elapsed_time(b2), 3)  # ms for 1000 calls == us per call
+        A2m = A2b.view(torch.float16).view(m2, n2)
+        out2 = torch.empty(m2, dtype=torch.float16, device=dev)
+        xv2 = x2.view(torch.float16)
+        for _ in range(20):
+            torch.mv(A2m, xv2, out=out2)
+        torch.cuda.synchronize()
+        a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a2.record(stream)
+        for _ in range(1000):
+            torch.mv(A2m, xv2, out=out2)
+        b2.record(stream)
+        b2.synchronize()
+        l2res["cublas_torch_mv_us"] = round(a2.elapsed_time(b2), 3)
+        l2res["aware_gbs"] = round((m2 * n2 * 2 + n2 * 2 + m2 * 2) / (l2res["aware_us"] * 1e-6) / 1e9, 1)
+        plan2.close()
+        del raw2
+
     # End to end through the public API: pinned x in, y out, every step.
     x_host = torch.empty_like(x, device="cpu").pin_memory()
     x_host.copy_(x)
@@ -393,7 +440,7 @@ def run_ours(args, rank, world, local):
                        "dtype_in": DT_NAME[dt], "dtype_out": DT_NAME[dt], "rows_per_gpu": m_loc,
                        "parallelism": f"row-shard x{world}" + (", NCCL broadcast(x) + all_gather(y)" if world > 1 else ""),
                        "mode": "aware", "l2": f"inputs larger than L2 ({a_bytes / 2**20:.0f} MiB of A per GPU), no flush"},
-            "modes_us": modes_us, "aware_speedup_vs_oblivious": ratio,
+            "modes_us": modes_us, "aware_speedup_vs_oblivious": ratio, "l2_resident": l2res,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src,
                          "frac_of_spec_8TBs": round(achieved / SPEC_HBM_GBS, 4), "kernel_us": round(kern_ms * 1e3, 3),

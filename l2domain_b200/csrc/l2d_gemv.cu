@@ -67,6 +67,8 @@ struct GemvArgs {
     int n_slots;
     int n_dom0;
     int n_dom1;
+    int64_t rows_split;           // rows [rows_split, rows_total) are whole rows of group big_grp
+    int big_grp;                  // the group with more SMs (takes the spill rows)
     unsigned long long *pair;     // [rows_total] packed partial pair, zero between calls
     unsigned long long *claim;    // [n_slots] epoch of the last claim
     unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims
@@ -223,9 +225,11 @@ __device__ __forceinline__ const uint8_t *stage_x(const GemvArgs &a, uint8_t *sm
     return smem;
 }
 
-template <int DT_IN, int DT_OUT, bool SPLIT>
+template <int DT_IN, int DT_OUT, bool SPLIT_T>
 __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp, int lane, const uint8_t *xs,
                                          int64_t xs_b0) {
+    // Spill rows (balance between unequal domain groups) are taken whole by the bigger group.
+    const bool SPLIT = SPLIT_T && row < a.rows_split;
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
     constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
     const int64_t b = row / a.M;
@@ -315,13 +319,26 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp
 template <int DT_IN, int DT_OUT, bool SPLIT>
 __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem) {
     int grp = 0, idx = slot, n_group = a.n_slots;
+    int64_t r0, r1;
     if (SPLIT) {
         grp = slot >= a.n_dom0;
         idx = grp ? slot - a.n_dom0 : slot;
         n_group = grp ? a.n_dom1 : a.n_dom0;
+        const int64_t Rs = a.rows_split, R = a.rows_total;
+        if (grp != a.big_grp || Rs == R) {  // the small group never sees the spill rows
+            r0 = Rs * idx / n_group;
+            r1 = Rs * (idx + 1) / n_group;
+        } else {
+            // Cost in half rows: a split row costs 1, a spill row (whole) costs 2.
+            const int64_t C2 = Rs + 2 * (R - Rs);
+            const int64_t c0 = C2 * idx / n_group, c1 = C2 * (idx + 1) / n_group;
+            r0 = c0 <= Rs ? c0 : Rs + (c0 - Rs + 1) / 2;
+            r1 = c1 <= Rs ? c1 : Rs + (c1 - Rs + 1) / 2;
+        }
+    } else {
+        r0 = a.rows_total * idx / n_group;
+        r1 = a.rows_total * (idx + 1) / n_group;
     }
-    const int64_t r0 = a.rows_total * idx / n_group;
-    const int64_t r1 = a.rows_total * (idx + 1) / n_group;
     if (r0 >= r1) return;
     const uint8_t *xs = nullptr;
     int64_t b0 = 0;
@@ -333,10 +350,25 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
 
-// Claims the first slot whose claim epoch is older than E (any domain); -1 if none is left.
-__device__ __forceinline__ int claim_any(const GemvArgs &a, unsigned long long E) {
-    for (int t = 0; t < a.n_slots; ++t)
-        if (atomicMax(a.claim + t, E) < E) return t;
+__device__ __forceinline__ unsigned long long ld_claim(const unsigned long long *p) {
+    return *reinterpret_cast<const volatile unsigned long long *>(p);
+}
+
+// Warp-wide search for an unclaimed slot (epoch older than E): 32 slots are read per step and only
+// candidates are tried with atomicMax.  Returns the slot won, or -1 when none is left.
+__device__ __forceinline__ int warp_claim_any(const GemvArgs &a, unsigned long long E, int lane) {
+    for (int base = 0; base < a.n_slots; base += 32) {
+        const int t = base + lane;
+        const bool cand = t < a.n_slots && ld_claim(a.claim + t) < E;
+        uint32_t m = __ballot_sync(0xffffffffu, cand);
+        while (m) {
+            const int l = __ffs(m) - 1;
+            m &= m - 1;
+            int ok = 0;
+            if (lane == l) ok = atomicMax(a.claim + t, E) < E;
+            if (__shfl_sync(0xffffffffu, ok, l)) return base + l;
+        }
+    }
     return -1;
 }
 
@@ -345,21 +377,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int s_slot;
     __shared__ int s_last;
+    __shared__ int s_count;
+    __shared__ int s_list[kMaxSmid];
     __shared__ unsigned long long s_epoch;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
-    if (tid == 0) {
-        const unsigned long long E = *reinterpret_cast<volatile unsigned long long *>(a.ctl) + 1ull;
-        s_epoch = E;
-        const uint32_t sm = dev::smid();
-        const int home = sm < static_cast<uint32_t>(kMaxSmid) ? a.sm_slot[sm] : -1;
+    if (warp == 0) {
+        const unsigned long long E = ld_claim(a.ctl) + 1ull;
         int got = -1;
-        if (home >= 0 && atomicMax(a.claim + home, E) < E) {
-            got = home;
-        } else {
-            got = claim_any(a, E);
-            if (got >= 0) atomicAdd(a.ctl + 2, 1ull);
+        if (lane == 0) {
+            const uint32_t sm = dev::smid();
+            const int home = sm < static_cast<uint32_t>(kMaxSmid) ? a.sm_slot[sm] : -1;
+            if (home >= 0 && atomicMax(a.claim + home, E) < E) got = home;
         }
-        s_slot = got;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (got < 0) {  // this SM's slot is taken (two CTAs on one SM): any unclaimed slot will do
+            got = warp_claim_any(a, E, lane);
+            if (got >= 0 && lane == 0) atomicAdd(a.ctl + 2, 1ull);
+        }
+        if (lane == 0) {
+            s_slot = got;
+            s_epoch = E;
+            s_count = 0;
+        }
     }
     __syncthreads();
     if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT>(a, s_slot, warp, nwarps, lane, smem);
@@ -371,23 +410,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     }
     __syncthreads();
     if (!s_last) return;
-    // Last CTA: slots whose SM never hosted a CTA of this launch.
-    for (;;) {
-        if (tid == 0) {
-            const int got = claim_any(a, s_epoch);
-            if (got >= 0) atomicAdd(a.ctl + 2, 1ull);
-            s_slot = got;
-        }
-        __syncthreads();
-        const int t = s_slot;
-        if (t < 0) break;
-        run_slot<DT_IN, DT_OUT, SPLIT>(a, t, warp, nwarps, lane, smem);
+    // Last CTA: slots whose SM never hosted a CTA of this launch, found by one parallel sweep.
+    const unsigned long long E = s_epoch;
+    for (int t = tid; t < a.n_slots; t += blockDim.x) {
+        if (ld_claim(a.claim + t) < E && atomicMax(a.claim + t, E) < E) s_list[atomicAdd(&s_count, 1)] = t;
+    }
+    __syncthreads();
+    const int n_left = s_count;
+    if (tid == 0 && n_left) atomicAdd(a.ctl + 2, static_cast<unsigned long long>(n_left));
+    for (int k = 0; k < n_left; ++k) {
+        run_slot<DT_IN, DT_OUT, SPLIT>(a, s_list[k], warp, nwarps, lane, smem);
         __syncthreads();
     }
     if (tid == 0) {
         a.ctl[1] = 0ull;
         __threadfence();
-        *reinterpret_cast<volatile unsigned long long *>(a.ctl) = s_epoch;
+        *reinterpret_cast<volatile unsigned long long *>(a.ctl) = E;
     }
 }
 
@@ -696,19 +734,14 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         delete p;
         return set_error(L2D_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e));
     }
-    // x staging: the most problems any slot's rows span, times the padded row length.
+    // x staging: the most problems any slot's rows can span.  Every slot partition (all SMs, one
+    // domain group, or the bigger group with spill rows) gives a slot at most ~2R/n_min + 1
+    // contiguous rows, and k contiguous rows touch at most ceil(k / M) + 1 problems.
     if (p->rows_total > 0 && d.N > 0) {
-        int64_t max_nb = 0;
-        std::vector<int> groups{p->n_slots};
-        if (p->has_domains) {
-            groups.push_back(p->n_dom[0]);
-            groups.push_back(p->n_dom[1]);
-        }
-        for (int n : groups)
-            for (int i = 0; i < n; ++i) {
-                int64_t r0 = p->rows_total * i / n, r1 = p->rows_total * (i + 1) / n;
-                if (r1 > r0) max_nb = std::max<int64_t>(max_nb, (r1 - 1) / d.M - r0 / d.M + 1);
-            }
+        int n_min = p->n_slots;
+        if (p->has_domains) n_min = std::min({n_min, p->n_dom[0], p->n_dom[1]});
+        const int64_t max_rows = 2 * p->rows_total / std::max(n_min, 1) + 2;
+        const int64_t max_nb = std::min<int64_t>(d.batch, (max_rows + d.M - 1) / d.M + 1);
         const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
         if (max_nb * rb16 <= kXSmemMax) p->x_smem_bytes = static_cast<size_t>(max_nb * rb16);
     }
@@ -776,6 +809,15 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     a.n_dom1 = p->n_dom[1];
     a.pair = p->d_pair;
     a.x_smem = p->x_smem_bytes > 0;
+    // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes
+    // whole rows [Rs, R), Rs = 2 n_small R / (n_small + n_big), so every SM streams the same bytes.
+    // The swapped control stays pure (no spill).
+    a.big_grp = p->n_dom[1] > p->n_dom[0] ? 1 : 0;
+    a.rows_split = p->rows_total;
+    if (split && mode != L2D_MODE_SWAPPED && p->n_dom[0] != p->n_dom[1] && p->n_dom[0] > 0 && p->n_dom[1] > 0) {
+        const int64_t ns = std::min(p->n_dom[0], p->n_dom[1]), nb = std::max(p->n_dom[0], p->n_dom[1]);
+        a.rows_split = (2 * ns * p->rows_total + (ns + nb) / 2) / (ns + nb);
+    }
     a.claim = p->d_claim;
     a.ctl = p->d_ctl;
     KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split);
