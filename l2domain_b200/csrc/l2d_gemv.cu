@@ -225,9 +225,31 @@ __device__ __forceinline__ const uint8_t *stage_x(const GemvArgs &a, uint8_t *sm
     return smem;
 }
 
+// A row whose pair atomic has been issued by lane 0 but whose returned value is not inspected
+// yet.  It is resolved after the warp has issued the next row's first loads, so the atomic's round
+// trip overlaps with memory traffic instead of stalling the warp.
+struct Pending {
+    unsigned long long old;
+    uint8_t *yp;
+    int64_t row;
+    float sum;
+    int grp;
+    bool active;
+};
+
+template <int DT_OUT> __device__ __forceinline__ void resolve(const GemvArgs &a, Pending &p) {
+    if (!p.active) return;
+    p.active = false;
+    const uint32_t other = static_cast<uint32_t>(p.old >> (32 * (p.grp ^ 1)));
+    if (other != 0u) {
+        store_out<DT_OUT>(p.yp, p.sum + __uint_as_float(~other));  // commutative: same bits either way
+        a.pair[p.row] = 0ull;
+    }
+}
+
 template <int DT_IN, int DT_OUT, bool SPLIT_T>
 __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp, int lane, const uint8_t *xs,
-                                         int64_t xs_b0) {
+                                         int64_t xs_b0, Pending &pend) {
     // Spill rows (balance between unequal domain groups) are taken whole by the bigger group.
     const bool SPLIT = SPLIT_T && row < a.rows_split;
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
@@ -249,7 +271,7 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp
     const uint8_t *abase = a.region_base + lane * 32;
     const int64_t xoff0 = static_cast<int64_t>(lane) * 32 - static_cast<int64_t>(rs);
     Acc<DT_IN> acc;
-    bool saw_mine = false, saw_other = false;
+    bool saw_mine = false, saw_other = false, resolved = false;
     for (uint64_t ub = u0; ub < u1; ub += 64) {
         const uint64_t ua = ub + lane, uc = ub + 32 + lane;
         const bool ina = ua < u1, inc = uc < u1;
@@ -277,6 +299,10 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u)
                 if (idx[u] >= 0) av[u] = ld_stream32(abase + ((ub + idx[u]) << kUnitShift));
+            if (!resolved) {
+                if (lane == 0) resolve<DT_OUT>(a, pend);
+                resolved = true;
+            }
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
                 if (idx[u] >= 0) {
@@ -306,14 +332,14 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp
     }
     // Both domain groups own part of this row.  Each adds ~bits(partial) into its own 32-bit half
     // of the row's pair word; ~bits is never 0 for a value arithmetic produces, so the group that
-    // finds the other half non-zero holds both partials and finishes the row.
-    const unsigned long long mine = static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp);
-    const unsigned long long old = atomicAdd(a.pair + row, mine);
-    const uint32_t other = static_cast<uint32_t>(old >> (32 * (grp ^ 1)));
-    if (other != 0u) {
-        store_out<DT_OUT>(yp, sum + __uint_as_float(~other));  // commutative: same bits either way
-        a.pair[row] = 0ull;
-    }
+    // finds the other half non-zero holds both partials and finishes the row (in resolve()).
+    if (!resolved) resolve<DT_OUT>(a, pend);
+    pend.old = atomicAdd(a.pair + row, static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp));
+    pend.yp = yp;
+    pend.row = row;
+    pend.sum = sum;
+    pend.grp = grp;
+    pend.active = true;
 }
 
 template <int DT_IN, int DT_OUT, bool SPLIT>
@@ -346,7 +372,11 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
         b0 = r0 / a.M;
         xs = stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
     }
-    for (int64_t row = r0 + warp; row < r1; row += nwarps) gemv_row<DT_IN, DT_OUT, SPLIT>(a, row, grp, lane, xs, b0);
+    Pending pend;
+    pend.active = false;
+    for (int64_t row = r0 + warp; row < r1; row += nwarps)
+        gemv_row<DT_IN, DT_OUT, SPLIT>(a, row, grp, lane, xs, b0, pend);
+    if (lane == 0) resolve<DT_OUT>(a, pend);
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
 

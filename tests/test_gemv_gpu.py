@@ -161,15 +161,21 @@ def test_integer_kat_half_types(dev, dt):
 
 
 def test_aware_and_swapped_bit_identical_and_deterministic(dev):
-    """Swapping which SMs take which windows changes no arithmetic: the two per-row partials are
-    the same sums, combined commutatively.  Repeated calls are bit-identical."""
+    """Swapping which SMs take which units changes no arithmetic on split rows: the two per-row
+    partials are the same sums, combined commutatively.  (AWARE also hands the bigger domain
+    group the last rows whole, to balance 70/78 SMs; SWAPPED does not, so only rows below that
+    point are compared.)  Repeated calls are bit-identical."""
     M, N = 1024, 8192
     A, x = host_inputs(M, N, L.F16)
     outs, stats = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED])
-    assert np.array_equal(outs[L.MODE_AWARE], outs[L.MODE_SWAPPED])
+    n0, n1 = stats["domain_sms"]
+    ns, nb = min(n0, n1), max(n0, n1)
+    rs = M if ns == nb else (2 * ns * M + (ns + nb) // 2) // (ns + nb)
+    assert 0 < rs <= M
+    assert np.array_equal(outs[L.MODE_AWARE][:rs], outs[L.MODE_SWAPPED][:rs])
     outs2, _ = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE])
     assert np.array_equal(outs[L.MODE_AWARE], outs2[L.MODE_AWARE])
-    assert stats["calls"] == 2 and stats["domain_sms"][0] > 0 and stats["domain_sms"][1] > 0
+    assert stats["calls"] == 2 and n0 > 0 and n1 > 0
 
 
 def test_device_generators_match_oracle(dev):
