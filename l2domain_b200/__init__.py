@@ -112,6 +112,7 @@ SIGNATURES = {
     "l2d_gemv": (_i, [_vp, _vp, _vp, _vp, _i, _vp]),
     "l2d_plan_stats_get": (_i, [_vp, C.POINTER(PlanStats)]),
     "l2d_plan_domain_map": (_i, [_vp, _pi, _i, _pi, _pu32]),
+    "l2d_gemv_noalloc": (_i, [C.POINTER(GemvDesc), C.POINTER(DomainMap), _vp, _vp, _i, _vp]),
     "l2d_fill_ref": (_i, [_vp, _i, _u64, _u64, _u32, _i, _i, _vp]),
     "l2d_fill_cfg": (_i, [_vp, _i, _u64, _u64, _u64, _u64, _i, C.c_float, C.c_float, _vp]),
     "l2d_l2_flush": (_i, [_i, _vp]),

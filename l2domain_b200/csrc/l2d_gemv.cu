@@ -900,3 +900,197 @@ int l2d_plan_domain_map(const l2d_plan *p, int *sm_domain, int cap, int *num_sm,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot call cudaMalloc when they need a GEMV: a serving runtime that reserves nearly
+// all HBM for its own pools at start-up and forbids later allocations, code running between
+// cudaStreamBeginCapture and cudaStreamEndCapture (a cudaMalloc there breaks the capture), or a
+// latency-critical path that must not enter the allocator.  l2d_gemv_noalloc runs the same kernel
+// as l2d_gemv without a plan: its scratch (control words, slot claims, the SM->slot table, the
+// attr bits and one pair word per row) lives in the file-scope array below, which every GPU that
+// loads this library holds until the process exits.  Limits: L2D_NOALLOC_MAX_ROWS rows over all
+// problems, L2D_NOALLOC_MAX_PAGES 2 MiB pages of A.  Every call shares the array and leaves its
+// contents for the next call (the pair words return to zero when a call completes), so calls
+// that overlap on the GPU (other streams, other threads) race and must be serialised by the
+// caller.
+// ---------------------------------------------------------------------------------------------
+
+namespace l2d {
+namespace noalloc {
+
+constexpr size_t kCtlOff = 0;
+constexpr size_t kClaimOff = 256;
+constexpr size_t kSlotOff = kClaimOff + kMaxSmid * sizeof(unsigned long long);
+constexpr size_t kAttrOff = kSlotOff + kMaxSmid * sizeof(int32_t);
+constexpr size_t kPairOff = kAttrOff + (L2D_NOALLOC_MAX_PAGES / 32) * sizeof(uint32_t);
+constexpr size_t kBytes = kPairOff + static_cast<size_t>(L2D_NOALLOC_MAX_ROWS) * sizeof(unsigned long long);
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_scratch[kBytes];
+
+std::mutex g_mu;
+uint8_t *g_ptr[kMaxDevices] = {nullptr};
+
+// First call on a device: the device address of g_scratch (host code may not use the symbol
+// itself as a pointer) and one clear of the whole array.  Runs with `device` current.
+int setup(int device, uint8_t **out) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ptr[device]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+        if (e != cudaSuccess || !p)
+            return set_error(L2D_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+        e = cudaMemset(p, 0, kBytes);
+        if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "clearing the static scratch: %s", cudaGetErrorString(e));
+        e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "clearing the static scratch: %s", cudaGetErrorString(e));
+        g_ptr[device] = static_cast<uint8_t *>(p);
+    }
+    *out = g_ptr[device];
+    return L2D_OK;
+}
+
+}  // namespace noalloc
+}  // namespace l2d
+
+extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, const void *x, void *y,
+                                int mode, void *stream) {
+    using namespace l2d;
+    clear_error();
+    if (!desc_in) return set_error(L2D_ERR_INVALID, "gemv_noalloc: null descriptor");
+    l2d_gemv_desc d = *desc_in;
+    if (d.M < 0 || d.N < 0 || !valid_dtype(d.dtype_in) || !valid_dtype(d.dtype_out))
+        return set_error(L2D_ERR_INVALID, "gemv_noalloc: bad shape or dtype");
+    if (mode < L2D_MODE_OBLIVIOUS || mode > L2D_MODE_STREAM) return set_error(L2D_ERR_INVALID, "bad mode %d", mode);
+    if (d.lda == 0) d.lda = d.N;
+    if (d.batch <= 0) d.batch = 1;
+    if (d.stride_a == 0) d.stride_a = d.M * d.lda;
+    if (d.stride_x == 0) d.stride_x = d.N;
+    if (d.stride_y == 0) d.stride_y = d.M;
+    if (d.lda < d.N || (d.batch > 1 && (d.stride_a < d.M * d.lda || d.stride_x < d.N || d.stride_y < d.M)))
+        return set_error(L2D_ERR_INVALID, "gemv_noalloc: lda or strides too small");
+    const int64_t R = d.batch * d.M;
+    if (R > L2D_NOALLOC_MAX_ROWS)
+        return set_error(L2D_ERR_INVALID, "gemv_noalloc: %lld rows exceed the allocation-free limit of %d rows",
+                         (long long)R, L2D_NOALLOC_MAX_ROWS);
+    if (R == 0) return L2D_OK;
+    const int eb = elem_bytes(d.dtype_in), eo = elem_bytes(d.dtype_out);
+    if (((d.lda * eb) & 15) || (d.batch > 1 && (((d.stride_a * eb) & 15) || ((d.stride_x * eb) & 15))))
+        return set_error(L2D_ERR_UNSUPPORTED, "lda, stride_a and stride_x must be multiples of 16 bytes");
+    if ((reinterpret_cast<uintptr_t>(d.A) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
+        return set_error(L2D_ERR_UNSUPPORTED, "A and x must be 16-byte aligned");
+    if (!d.A || !x || !y || (reinterpret_cast<uintptr_t>(y) & (eo - 1)))
+        return set_error(L2D_ERR_INVALID, "null or misaligned A, x or y");
+    const bool split = mode != L2D_MODE_STREAM && d.N > 0;
+    if (split && (!map || !map->sm_domain || !map->attr))
+        return set_error(L2D_ERR_UNSUPPORTED, "gemv_noalloc: modes other than STREAM need a domain map");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return set_error(L2D_ERR_NO_DEVICE, "no CUDA device");
+    if (d.device < 0 || d.device >= ndev || d.device >= noalloc::kMaxDevices)
+        return set_error(L2D_ERR_INVALID, "device %d out of range", d.device);
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != d.device) L2D_CUDA_TRY(cudaSetDevice(d.device));
+    struct Restore {
+        int prev, dev;
+        ~Restore() {
+            if (prev >= 0 && prev != dev) cudaSetDevice(prev);
+        }
+    } restore{prev, d.device};
+    int num_sm = 0;
+    L2D_CUDA_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, d.device));
+    uint8_t *scratch = nullptr;
+    int st = noalloc::setup(d.device, &scratch);
+    if (st != L2D_OK) return st;
+
+    // Host tables on the stack: SM -> slot and the attr bits of the pages A's rows touch.
+    const uint64_t A = reinterpret_cast<uint64_t>(d.A);
+    const uint64_t span = static_cast<uint64_t>(((R - 1) / d.M * d.stride_a + (R - 1) % d.M * d.lda + d.N) * eb);
+    int32_t slot[kMaxSmid];
+    uint32_t attr_bits[L2D_NOALLOC_MAX_PAGES / 32];
+    int n_dom[2] = {0, 0};
+    size_t attr_words = 1;
+    attr_bits[0] = 0;
+    const uint8_t *region = reinterpret_cast<const uint8_t *>(A & ~uint64_t(1023));
+    uint32_t mask = 0;
+    int gran_shift = kPageShift;
+    for (int s = 0; s < kMaxSmid; ++s) slot[s] = -1;
+    if (split) {
+        if (map->num_sm != num_sm) return set_error(L2D_ERR_INVALID, "domain map has %d SMs, device has %d",
+                                                    map->num_sm, num_sm);
+        const uint64_t base = reinterpret_cast<uint64_t>(map->base);
+        if (base % kPageBytes || base > A || A + span > base + map->num_pages * kPageBytes)
+            return set_error(L2D_ERR_INVALID, "domain map region does not cover A");
+        if (map->num_pages > static_cast<size_t>(L2D_NOALLOC_MAX_PAGES))
+            return set_error(L2D_ERR_INVALID, "gemv_noalloc: %zu pages exceed the limit of %d", map->num_pages,
+                             L2D_NOALLOC_MAX_PAGES);
+        int next[2] = {0, 0};
+        for (int s = 0; s < num_sm; ++s) n_dom[map->sm_domain[s] & 1]++;
+        if (n_dom[0] == 0 || n_dom[1] == 0) return set_error(L2D_ERR_INVALID, "domain map has an empty domain");
+        next[1] = n_dom[0];
+        for (int s = 0; s < num_sm; ++s) slot[s] = next[map->sm_domain[s] & 1]++;
+        attr_words = (map->num_pages + 31) / 32;
+        for (size_t w = 0; w < attr_words; ++w) attr_bits[w] = 0;
+        for (size_t i = 0; i < map->num_pages; ++i)
+            if (map->attr[i] & 1) attr_bits[i / 32] |= 1u << (i % 32);
+        region = reinterpret_cast<const uint8_t *>(base);
+        mask = map->mask;
+        gran_shift = lowest_bit_or(mask, kPageShift);
+    } else {
+        for (int s = 0; s < num_sm && s < kMaxSmid; ++s) slot[s] = s;
+    }
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    L2D_CUDA_TRY(cudaMemcpyAsync(scratch + noalloc::kSlotOff, slot, sizeof slot, cudaMemcpyHostToDevice, cs));
+    L2D_CUDA_TRY(cudaMemcpyAsync(scratch + noalloc::kAttrOff, attr_bits, attr_words * sizeof(uint32_t),
+                                 cudaMemcpyHostToDevice, cs));
+
+    GemvArgs a;
+    a.A = static_cast<const uint8_t *>(d.A);
+    a.x = static_cast<const uint8_t *>(x);
+    a.y = static_cast<uint8_t *>(y);
+    a.M = d.M;
+    a.row_bytes = d.N * eb;
+    a.lda_bytes = d.lda * eb;
+    a.stride_a_bytes = d.stride_a * eb;
+    a.stride_x_bytes = d.stride_x * eb;
+    a.stride_y_elems = d.stride_y;
+    a.rows_total = R;
+    a.region_base = region;
+    a.attr_bits = reinterpret_cast<const uint32_t *>(scratch + noalloc::kAttrOff);
+    a.mask = mask;
+    a.gran_shift = gran_shift;
+    a.dom_kind = mode == L2D_MODE_OBLIVIOUS ? 1 : 0;
+    a.flip = mode == L2D_MODE_SWAPPED ? 1 : 0;
+    a.sm_slot = reinterpret_cast<const int32_t *>(scratch + noalloc::kSlotOff);
+    a.n_slots = num_sm;
+    a.n_dom0 = n_dom[0];
+    a.n_dom1 = n_dom[1];
+    a.pair = reinterpret_cast<unsigned long long *>(scratch + noalloc::kPairOff);
+    a.claim = reinterpret_cast<unsigned long long *>(scratch + noalloc::kClaimOff);
+    a.ctl = reinterpret_cast<unsigned long long *>(scratch + noalloc::kCtlOff);
+    a.big_grp = n_dom[1] > n_dom[0] ? 1 : 0;
+    a.rows_split = R;
+    if (split && mode != L2D_MODE_SWAPPED && n_dom[0] != n_dom[1]) {
+        const int64_t ns = std::min(n_dom[0], n_dom[1]), nb = std::max(n_dom[0], n_dom[1]);
+        a.rows_split = (2 * ns * R + (ns + nb) / 2) / (ns + nb);
+    }
+    // x staging, sized as l2d_plan_create sizes it.
+    size_t x_smem = 0;
+    if (d.N > 0) {
+        int n_min = num_sm;
+        if (split) n_min = std::min({n_min, n_dom[0], n_dom[1]});
+        const int64_t max_rows = 2 * R / std::max(n_min, 1) + 2;
+        const int64_t max_nb = std::min<int64_t>(d.batch, (max_rows + d.M - 1) / d.M + 1);
+        const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
+        if (max_nb * rb16 <= kXSmemMax) x_smem = static_cast<size_t>(max_nb * rb16);
+    }
+    a.x_smem = x_smem > 0;
+    KernelFn k = pick_kernel(d.dtype_in, d.dtype_out, split);
+    if (x_smem > 48 * 1024)
+        L2D_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(x_smem)));
+    k<<<num_sm, kThreads, x_smem, cs>>>(a);
+    L2D_CUDA_TRY(cudaGetLastError());
+    return L2D_OK;
+}
