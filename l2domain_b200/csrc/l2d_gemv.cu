@@ -67,8 +67,9 @@ struct GemvArgs {
     int n_slots;
     int n_dom0;
     int n_dom1;
-    int64_t rows_split;           // rows [rows_split, rows_total) are whole rows of group big_grp
-    int big_grp;                  // the group with more SMs (takes the spill rows)
+    int64_t spill_num;            // row r is a spill row iff floor((r+1)*num/den) > floor(r*num/den)
+    int64_t spill_den;            // (spill rows are taken whole by big_grp; num = 0: no spill rows)
+    int big_grp;                  // the group with more SMs
     unsigned long long *pair;     // [rows_total] packed partial pair, zero between calls
     unsigned long long *claim;    // [n_slots] epoch of the last claim
     unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims
@@ -225,6 +226,40 @@ __device__ __forceinline__ const uint8_t *stage_x(const GemvArgs &a, uint8_t *sm
     return smem;
 }
 
+// Balance between unequal domain groups: a fraction (n_big - n_small)/(n_big + n_small) of the rows,
+// spread evenly, is taken whole by the bigger group; the smaller group skips them.
+__device__ __forceinline__ bool spill_row(const GemvArgs &a, int64_t r) {
+    return a.spill_num != 0 && (r + 1) * a.spill_num / a.spill_den != r * a.spill_num / a.spill_den;
+}
+
+__device__ __forceinline__ void row_geometry(const GemvArgs &a, int64_t row, int64_t &b, int64_t &i) {
+    if (a.M == a.rows_total) {
+        b = 0;
+        i = row;
+    } else {
+        b = row / a.M;
+        i = row - b * a.M;
+    }
+}
+
+// Bulk L2 prefetch (one TMA request per 1 KiB unit) of the units of `row` this group will stream,
+// issued one row ahead so that the row's loads are L2 hits.  In the split modes only the group's
+// own units are fetched, so the prefetched lines are homed in the SM's own L2 half.
+__device__ __forceinline__ void prefetch_row(const GemvArgs &a, int64_t row, int grp, bool split, int lane) {
+    int64_t b, i;
+    row_geometry(a, row, b, i);
+    const uint64_t rs = static_cast<uint64_t>(a.A + b * a.stride_a_bytes + i * a.lda_bytes - a.region_base);
+    const uint64_t re = rs + static_cast<uint64_t>(a.row_bytes);
+    const uint64_t u0 = (rs + (1u << kUnitShift) - 1) >> kUnitShift;  // first full unit
+    const uint64_t u1 = re >> kUnitShift;                              // end of full units
+    for (uint64_t u = u0 + lane; u < u1; u += 32) {
+        if (split && unit_dom(a, u) != grp) continue;
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.region_base + (u << kUnitShift)),
+                     "r"(1u << kUnitShift)
+                     : "memory");
+    }
+}
+
 // A row whose pair atomic has been issued by lane 0 but whose returned value is not inspected
 // yet.  It is resolved after the warp has issued the next row's first loads, so the atomic's round
 // trip overlaps with memory traffic instead of stalling the warp.
@@ -251,11 +286,11 @@ template <int DT_IN, int DT_OUT, bool SPLIT_T>
 __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp, int lane, const uint8_t *xs,
                                          int64_t xs_b0, Pending &pend) {
     // Spill rows (balance between unequal domain groups) are taken whole by the bigger group.
-    const bool SPLIT = SPLIT_T && row < a.rows_split;
+    const bool SPLIT = SPLIT_T && !spill_row(a, row);
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
     constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
-    const int64_t b = row / a.M;
-    const int64_t i = row - b * a.M;
+    int64_t b, i;
+    row_geometry(a, row, b, i);
     const uint8_t *rowp = a.A + b * a.stride_a_bytes + i * a.lda_bytes;
     const bool xsm = xs != nullptr;
     const uint8_t *xrow = xsm ? xs + (b - xs_b0) * ((a.row_bytes + 15) & ~int64_t(15)) : a.x + b * a.stride_x_bytes;
@@ -345,26 +380,13 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp
 template <int DT_IN, int DT_OUT, bool SPLIT>
 __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem) {
     int grp = 0, idx = slot, n_group = a.n_slots;
-    int64_t r0, r1;
     if (SPLIT) {
         grp = slot >= a.n_dom0;
         idx = grp ? slot - a.n_dom0 : slot;
         n_group = grp ? a.n_dom1 : a.n_dom0;
-        const int64_t Rs = a.rows_split, R = a.rows_total;
-        if (grp != a.big_grp || Rs == R) {  // the small group never sees the spill rows
-            r0 = Rs * idx / n_group;
-            r1 = Rs * (idx + 1) / n_group;
-        } else {
-            // Cost in half rows: a split row costs 1, a spill row (whole) costs 2.
-            const int64_t C2 = Rs + 2 * (R - Rs);
-            const int64_t c0 = C2 * idx / n_group, c1 = C2 * (idx + 1) / n_group;
-            r0 = c0 <= Rs ? c0 : Rs + (c0 - Rs + 1) / 2;
-            r1 = c1 <= Rs ? c1 : Rs + (c1 - Rs + 1) / 2;
-        }
-    } else {
-        r0 = a.rows_total * idx / n_group;
-        r1 = a.rows_total * (idx + 1) / n_group;
     }
+    const int64_t r0 = a.rows_total * idx / n_group;
+    const int64_t r1 = a.rows_total * (idx + 1) / n_group;
     if (r0 >= r1) return;
     const uint8_t *xs = nullptr;
     int64_t b0 = 0;
@@ -374,8 +396,21 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     }
     Pending pend;
     pend.active = false;
-    for (int64_t row = r0 + warp; row < r1; row += nwarps)
+    // The smaller domain group skips the spill rows, which the bigger group takes whole.
+    const bool skip_spill = SPLIT && a.spill_num != 0 && grp != a.big_grp;
+    auto next_row = [&](int64_t r) {
+        r += nwarps;
+        while (skip_spill && r < r1 && spill_row(a, r)) r += nwarps;
+        return r;
+    };
+    int64_t row = r0 + warp;
+    if (skip_spill && row < r1 && spill_row(a, row)) row = next_row(row);
+    while (row < r1) {
+        const int64_t nxt = next_row(row);
+        if (nxt < r1) prefetch_row(a, nxt, grp, SPLIT && !spill_row(a, nxt), lane);
         gemv_row<DT_IN, DT_OUT, SPLIT>(a, row, grp, lane, xs, b0, pend);
+        row = nxt;
+    }
     if (lane == 0) resolve<DT_OUT>(a, pend);
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
@@ -839,14 +874,15 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     a.n_dom1 = p->n_dom[1];
     a.pair = p->d_pair;
     a.x_smem = p->x_smem_bytes > 0;
-    // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes
-    // whole rows [Rs, R), Rs = 2 n_small R / (n_small + n_big), so every SM streams the same bytes.
-    // The swapped control stays pure (no spill).
+    // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes a
+    // fraction (n_big - n_small)/(n_big + n_small) of the rows whole, spread evenly, so every SM
+    // streams the same bytes.  The swapped control stays pure (no spill rows).
     a.big_grp = p->n_dom[1] > p->n_dom[0] ? 1 : 0;
-    a.rows_split = p->rows_total;
+    a.spill_num = 0;
+    a.spill_den = 1;
     if (split && mode != L2D_MODE_SWAPPED && p->n_dom[0] != p->n_dom[1] && p->n_dom[0] > 0 && p->n_dom[1] > 0) {
-        const int64_t ns = std::min(p->n_dom[0], p->n_dom[1]), nb = std::max(p->n_dom[0], p->n_dom[1]);
-        a.rows_split = (2 * ns * p->rows_total + (ns + nb) / 2) / (ns + nb);
+        a.spill_num = std::abs(p->n_dom[1] - p->n_dom[0]);
+        a.spill_den = p->n_dom[0] + p->n_dom[1];
     }
     a.claim = p->d_claim;
     a.ctl = p->d_ctl;
@@ -1071,10 +1107,11 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
     a.claim = reinterpret_cast<unsigned long long *>(scratch + noalloc::kClaimOff);
     a.ctl = reinterpret_cast<unsigned long long *>(scratch + noalloc::kCtlOff);
     a.big_grp = n_dom[1] > n_dom[0] ? 1 : 0;
-    a.rows_split = R;
+    a.spill_num = 0;
+    a.spill_den = 1;
     if (split && mode != L2D_MODE_SWAPPED && n_dom[0] != n_dom[1]) {
-        const int64_t ns = std::min(n_dom[0], n_dom[1]), nb = std::max(n_dom[0], n_dom[1]);
-        a.rows_split = (2 * ns * R + (ns + nb) / 2) / (ns + nb);
+        a.spill_num = std::abs(n_dom[1] - n_dom[0]);
+        a.spill_den = n_dom[0] + n_dom[1];
     }
     // x staging, sized as l2d_plan_create sizes it.
     size_t x_smem = 0;

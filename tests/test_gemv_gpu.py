@@ -163,16 +163,17 @@ def test_integer_kat_half_types(dev, dt):
 def test_aware_and_swapped_bit_identical_and_deterministic(dev):
     """Swapping which SMs take which units changes no arithmetic on split rows: the two per-row
     partials are the same sums, combined commutatively.  (AWARE also hands the bigger domain
-    group the last rows whole, to balance 70/78 SMs; SWAPPED does not, so only rows below that
-    point are compared.)  Repeated calls are bit-identical."""
+    group an evenly spread fraction (n_big - n_small)/(n_big + n_small) of the rows whole, to
+    balance unequal SM counts; SWAPPED does not, so those rows are left out.)  Repeated calls
+    are bit-identical."""
     M, N = 1024, 8192
     A, x = host_inputs(M, N, L.F16)
     outs, stats = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED])
     n0, n1 = stats["domain_sms"]
-    ns, nb = min(n0, n1), max(n0, n1)
-    rs = M if ns == nb else (2 * ns * M + (ns + nb) // 2) // (ns + nb)
-    assert 0 < rs <= M
-    assert np.array_equal(outs[L.MODE_AWARE][:rs], outs[L.MODE_SWAPPED][:rs])
+    num, den = abs(n1 - n0), n0 + n1
+    split_rows = np.array([num == 0 or (r + 1) * num // den == r * num // den for r in range(M)])
+    assert split_rows.sum() > M // 2
+    assert np.array_equal(outs[L.MODE_AWARE][split_rows], outs[L.MODE_SWAPPED][split_rows])
     outs2, _ = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE])
     assert np.array_equal(outs[L.MODE_AWARE], outs2[L.MODE_AWARE])
     assert stats["calls"] == 2 and n0 > 0 and n1 > 0
