@@ -242,24 +242,6 @@ __device__ __forceinline__ void row_geometry(const GemvArgs &a, int64_t row, int
     }
 }
 
-// Bulk L2 prefetch (one TMA request per 1 KiB unit) of the units of `row` this group will stream,
-// issued one row ahead so that the row's loads are L2 hits.  In the split modes only the group's
-// own units are fetched, so the prefetched lines are homed in the SM's own L2 half.
-__device__ __forceinline__ void prefetch_row(const GemvArgs &a, int64_t row, int grp, bool split, int lane) {
-    int64_t b, i;
-    row_geometry(a, row, b, i);
-    const uint64_t rs = static_cast<uint64_t>(a.A + b * a.stride_a_bytes + i * a.lda_bytes - a.region_base);
-    const uint64_t re = rs + static_cast<uint64_t>(a.row_bytes);
-    const uint64_t u0 = (rs + (1u << kUnitShift) - 1) >> kUnitShift;  // first full unit
-    const uint64_t u1 = re >> kUnitShift;                              // end of full units
-    for (uint64_t u = u0 + lane; u < u1; u += 32) {
-        if (split && unit_dom(a, u) != grp) continue;
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.region_base + (u << kUnitShift)),
-                     "r"(1u << kUnitShift)
-                     : "memory");
-    }
-}
-
 // A row whose pair atomic has been issued by lane 0 but whose returned value is not inspected
 // yet.  It is resolved after the warp has issued the next row's first loads, so the atomic's round
 // trip overlaps with memory traffic instead of stalling the warp.
@@ -407,7 +389,6 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     if (skip_spill && row < r1 && spill_row(a, row)) row = next_row(row);
     while (row < r1) {
         const int64_t nxt = next_row(row);
-        if (nxt < r1) prefetch_row(a, nxt, grp, SPLIT && !spill_row(a, nxt), lane);
         gemv_row<DT_IN, DT_OUT, SPLIT>(a, row, grp, lane, xs, b0, pend);
         row = nxt;
     }
