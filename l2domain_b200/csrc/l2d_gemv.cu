@@ -226,21 +226,36 @@ __device__ __forceinline__ const uint8_t *stage_x(const GemvArgs &a, uint8_t *sm
     return smem;
 }
 
-// Balance between unequal domain groups: a fraction (n_big - n_small)/(n_big + n_small) of the rows,
-// spread evenly, is taken whole by the bigger group; the smaller group skips them.
-__device__ __forceinline__ bool spill_row(const GemvArgs &a, int64_t r) {
-    return a.spill_num != 0 && (r + 1) * a.spill_num / a.spill_den != r * a.spill_num / a.spill_den;
-}
-
-__device__ __forceinline__ void row_geometry(const GemvArgs &a, int64_t row, int64_t &b, int64_t &i) {
-    if (a.M == a.rows_total) {
-        b = 0;
-        i = row;
-    } else {
-        b = row / a.M;
-        i = row - b * a.M;
+// Balance between unequal domain groups: a fraction num/den = (n_big - n_small)/(n_big + n_small) of
+// the rows, spread evenly, is taken whole by the bigger group and skipped by the smaller one.  Row r
+// is such a spill row iff floor((r+1) num/den) > floor(r num/den), i.e. iff (r num mod den) + num >=
+// den.  A warp walks its rows with a fixed stride, so it carries (r num mod den), the problem index
+// and the row within the problem incrementally: no division per row.
+struct RowIter {  // rows_total < 2^31 (checked when the call is set up)
+    int32_t row, b, i;
+    int32_t phase;  // row * num mod den
+    __device__ __forceinline__ void start(const GemvArgs &a, int32_t r) {
+        const int32_t M = static_cast<int32_t>(a.M);
+        row = r;
+        b = r / M;
+        i = r - b * M;
+        phase = a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(r) * a.spill_num % a.spill_den) : 0;
     }
-}
+    __device__ __forceinline__ void advance(const GemvArgs &a, int32_t stride, int32_t step_phase) {
+        const int32_t M = static_cast<int32_t>(a.M);
+        row += stride;
+        i += stride;
+        while (i >= M) {
+            i -= M;
+            ++b;
+        }
+        phase += step_phase;
+        if (phase >= a.spill_den) phase -= static_cast<int32_t>(a.spill_den);
+    }
+    __device__ __forceinline__ bool spill(const GemvArgs &a) const {
+        return a.spill_num != 0 && phase + a.spill_num >= a.spill_den;
+    }
+};
 
 // A row whose pair atomic has been issued by lane 0 but whose returned value is not inspected
 // yet.  It is resolved after the warp has issued the next row's first loads, so the atomic's round
@@ -264,15 +279,14 @@ template <int DT_OUT> __device__ __forceinline__ void resolve(const GemvArgs &a,
     }
 }
 
-template <int DT_IN, int DT_OUT, bool SPLIT_T>
-__device__ __forceinline__ void gemv_row(const GemvArgs &a, int64_t row, int grp, int lane, const uint8_t *xs,
-                                         int64_t xs_b0, Pending &pend) {
-    // Spill rows (balance between unequal domain groups) are taken whole by the bigger group.
-    const bool SPLIT = SPLIT_T && !spill_row(a, row);
+// One row of A for one domain group.  SPLIT: the row is shared by both groups (false for the
+// unsplit kernel and for spill rows, which the bigger group takes whole).
+template <int DT_IN, int DT_OUT>
+__device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool SPLIT, int grp, int lane,
+                                         const uint8_t *xs, int64_t xs_b0, Pending &pend) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
     constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
-    int64_t b, i;
-    row_geometry(a, row, b, i);
+    const int64_t row = it.row, b = it.b, i = it.i;
     const uint8_t *rowp = a.A + b * a.stride_a_bytes + i * a.lda_bytes;
     const bool xsm = xs != nullptr;
     const uint8_t *xrow = xsm ? xs + (b - xs_b0) * ((a.row_bytes + 15) & ~int64_t(15)) : a.x + b * a.stride_x_bytes;
@@ -379,18 +393,15 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     Pending pend;
     pend.active = false;
     // The smaller domain group skips the spill rows, which the bigger group takes whole.
-    const bool skip_spill = SPLIT && a.spill_num != 0 && grp != a.big_grp;
-    auto next_row = [&](int64_t r) {
-        r += nwarps;
-        while (skip_spill && r < r1 && spill_row(a, r)) r += nwarps;
-        return r;
-    };
-    int64_t row = r0 + warp;
-    if (skip_spill && row < r1 && spill_row(a, row)) row = next_row(row);
-    while (row < r1) {
-        const int64_t nxt = next_row(row);
-        gemv_row<DT_IN, DT_OUT, SPLIT>(a, row, grp, lane, xs, b0, pend);
-        row = nxt;
+    const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
+    const int32_t step_phase =
+        a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
+    RowIter it;
+    if (r0 + warp < r1) it.start(a, static_cast<int32_t>(r0 + warp));
+    for (int64_t row = r0 + warp; row < r1; row += nwarps, it.advance(a, nwarps, step_phase)) {
+        const bool spill = SPLIT && it.spill(a);
+        if (spill && small_grp) continue;
+        gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
     }
     if (lane == 0) resolve<DT_OUT>(a, pend);
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
@@ -646,8 +657,8 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
     if (d.stride_y == 0) d.stride_y = d.M;
     if (d.batch > 1 && (d.stride_a < d.M * d.lda || d.stride_x < d.N || d.stride_y < d.M))
         return set_error(L2D_ERR_INVALID, "batch strides overlap");
-    if (d.M > 0 && d.batch > (int64_t(1) << 40) / std::max<int64_t>(d.M, 1))
-        return set_error(L2D_ERR_INVALID, "batch * M too large");
+    if (d.M > 0 && d.batch > (int64_t(1) << 31) / std::max<int64_t>(d.M, 1) - 1)
+        return set_error(L2D_ERR_INVALID, "batch * M must stay below 2^31 rows");
     const int eb = elem_bytes(d.dtype_in);
     if (((d.lda * eb) & 15) || (d.batch > 1 && (((d.stride_a * eb) & 15) || ((d.stride_x * eb) & 15))))
         return set_error(L2D_ERR_UNSUPPORTED, "lda, stride_a and stride_x must be multiples of 16 bytes");
