@@ -710,6 +710,25 @@ KernelFn pick_kernel(int din, int dout, bool split) {
     }
 }
 
+// The kernels' dynamic shared-memory limit is process-wide state of each kernel, so it is raised once
+// per kernel and device to the device maximum (every launch then passes its own size) instead of
+// per plan, where a later plan with a smaller size would break an earlier plan's launches.
+int allow_max_smem(KernelFn k, int device) {
+    static std::mutex mu;
+    static std::vector<std::pair<KernelFn, int>> done;
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto &e : done)
+        if (e.first == k && e.second == device) return L2D_OK;
+    int optin = 0;
+    L2D_CUDA_TRY(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    cudaFuncAttributes fa;
+    L2D_CUDA_TRY(cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(k)));
+    L2D_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      optin - static_cast<int>(fa.sharedSizeBytes)));
+    done.emplace_back(k, device);
+    return L2D_OK;
+}
+
 // Shared memory of one launch: the warp rings plus the staged x when it fits (else x is read from
 // global memory and x_stride_f32 is 0).  nb = the most problems any slot's rows can span.
 size_t launch_smem(int64_t N, int64_t nb, int64_t *x_stride_f32) {
@@ -1018,13 +1037,11 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
                                                               std::max<int64_t>(d.M, 1) + 1);
         p->smem_bytes = launch_smem(d.N, max_nb, &p->x_stride_f32);
         for (bool split : {false, true}) {
-            cudaError_t fe = cudaFuncSetAttribute(pick_kernel(d.dtype_in, d.dtype_out, split),
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  static_cast<int>(p->smem_bytes));
-            if (fe != cudaSuccess) {
+            const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, split), d.device);
+            if (fe != L2D_OK) {
                 cudaFree(p->dev_block);
                 delete p;
-                return set_error(L2D_ERR_CUDA, "shared memory attribute: %s", cudaGetErrorString(fe));
+                return fe;
             }
         }
     }
@@ -1333,7 +1350,8 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
     a.x_smem = x_stride > 0;
     a.x_stride_f32 = x_stride;
     KernelFn k = pick_kernel(d.dtype_in, d.dtype_out, split);
-    L2D_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    st = allow_max_smem(k, d.device);
+    if (st != L2D_OK) return st;
     k<<<num_sm, kThreads, smem, cs>>>(a);
     L2D_CUDA_TRY(cudaGetLastError());
     return L2D_OK;

@@ -179,6 +179,32 @@ def test_aware_and_swapped_bit_identical_and_deterministic(dev):
     assert stats["calls"] == 2 and n0 > 0 and n1 > 0
 
 
+def test_plans_of_different_sizes_coexist(dev):
+    """A plan keeps working after another plan with a smaller shared-memory footprint is created
+    for the same element types (the kernels' shared-memory limit is process-wide state)."""
+    big_M, big_N, small_M, small_N = 512, 16384, 256, 1024
+    Ab, xb = host_inputs(big_M, big_N, L.F16)
+    As, xs = host_inputs(small_M, small_N, L.F16)
+    raw_b, A_b = aligned_empty(Ab.nbytes)
+    A_b.copy_(to_dev(Ab).view(torch.uint8).reshape(-1))
+    raw_s, A_s = aligned_empty(As.nbytes)
+    A_s.copy_(to_dev(As).view(torch.uint8).reshape(-1))
+    x_b, x_s = to_dev(xb), to_dev(xs)
+    plan_b = L.GemvPlan(A_b, big_M, big_N, L.F16, L.F32)
+    plan_s = L.GemvPlan(A_s, small_M, small_N, L.F16, L.F32)
+    y_b = torch.empty(big_M, device="cuda")
+    y_s = torch.empty(small_M, device="cuda")
+    for mode in ALL_MODES:
+        plan_b.gemv(A_b, x_b, y_b, mode)
+        plan_s.gemv(A_s, x_s, y_s, mode)
+        torch.cuda.synchronize()
+        check({mode: y_b.cpu().numpy()}, oracle_y(Ab, xb, L.F16, big_M, big_N, big_N, 1, L.F32), L.F16, L.F32, [mode])
+        check({mode: y_s.cpu().numpy()}, oracle_y(As, xs, L.F16, small_M, small_N, small_N, 1, L.F32), L.F16, L.F32,
+              [mode])
+    plan_b.close()
+    plan_s.close()
+
+
 def test_device_generators_match_oracle(dev):
     n = 1 << 20
     for dt in (L.F32, L.F16, L.BF16):
