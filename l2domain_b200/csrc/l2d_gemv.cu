@@ -12,13 +12,10 @@
 //    warp ballot, so no row lists are read.  The SMs of domain d stream exactly the units homed in
 //    d (AWARE), the other domain's (SWAPPED), or a pseudo-random half at the probed granule size
 //    (OBLIVIOUS); STREAM takes every unit of its rows.
-//  * Each warp runs a producer/consumer pipeline over its rows: the producer walks the units the
-//    group streams and issues them as cp.async copies (2 x 16 bytes per lane) into a per-warp ring
-//    of 12 x 1 KiB shared-memory slots; the consumer reads slot k while the next 11 units are in
-//    flight, so loads never drain at row boundaries and no register holds in-flight data.  x is
-//    staged once per CTA as fp32 in shared memory (swizzled so lanes read it without bank
-//    conflicts); A pairs are widened exactly (bf16: a shift and a mask; fp16: cvt) and multiplied
-//    with packed fma.rn.f32x2.
+//  * A lane moves 32 bytes per load (ld.global.nc.L1::no_allocate.v8.b32), U units in flight per
+//    warp, and multiplies with one mixed-precision FMA per element (fma.rn.f32.f16 / .bf16, exact
+//    f16/bf16 -> f32 products) or packed fma.rn.f32x2 for fp32; x sits in shared memory in its
+//    input type, loaded once per CTA.  This keeps the kernel far from the issue limit.
 //  * Per row, each domain group produces one fp32 partial.  Both partials travel inside one packed
 //    64-bit atomicAdd (each half holds ~bits(partial)): the group that sees the other half already
 //    present adds part[0] + part[1] (commutative, so deterministic) and stores y.  No fence, no
@@ -44,18 +41,15 @@
 namespace l2d {
 
 constexpr int kUnitShift = 10;  // 1 KiB units: 32 bytes per lane
-constexpr int kWarps = 12;
-constexpr int kThreads = kWarps * 32;
-constexpr int kRing = 12;       // units per warp ring; kRing - 1 are in flight while one is consumed
-constexpr int kRowRing = 16;    // row descriptors per warp (power of two, >= kRing + 2)
-constexpr int kSmemLimit = 227 * 1024;
+constexpr int kThreads = 512;
+constexpr int kUnroll = 8;      // units in flight per warp
+constexpr int kXSmemMax = 96 * 1024;
 
 struct GemvArgs {
     const uint8_t *A;
     const uint8_t *x;
     uint8_t *y;
     int64_t M;
-    int64_t N;
     int64_t row_bytes;
     int64_t lda_bytes;
     int64_t stride_a_bytes;
@@ -68,13 +62,12 @@ struct GemvArgs {
     int gran_shift;
     int dom_kind;                 // 0 = probed XOR model, 1 = hash of the granule index
     int flip;                     // 1 = swapped control
-    int x_smem;                   // 1 = x staged as fp32 in shared memory, 0 = read from global
-    int64_t x_stride_f32;         // floats between staged x vectors (multiple of 32)
+    int x_smem;                   // 1 = stage the slot's x vectors in shared memory
     const int32_t *sm_slot;       // [kMaxSmid] slot of each SM, -1 = none
     int n_slots;
     int n_dom0;
     int n_dom1;
-    int64_t spill_num;            // row r is a spill row iff (r*num mod den) + num >= den
+    int64_t spill_num;            // row r is a spill row iff floor((r+1)*num/den) > floor(r*num/den)
     int64_t spill_den;            // (spill rows are taken whole by big_grp; num = 0: no spill rows)
     int big_grp;                  // the group with more SMs
     unsigned long long *pair;     // [rows_total] packed partial pair, zero between calls
@@ -82,37 +75,27 @@ struct GemvArgs {
     unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims
 };
 
-// ---- per-warp shared-memory ring --------------------------------------------------------------
-
-struct RowDesc {           // one row of the warp's stream
-    int64_t rs;            // region-relative byte offset of the row start
-    int32_t row, b, i;     // global row, problem, row within the problem
-    int32_t flags;         // bit 0: this group owns units of the row, bit 1: the other group does,
-                           // bit 2: the row is split between the groups
-    int32_t pad[2];
+struct Vec32 {
+    uint32_t v[8];
 };
 
-struct UnitMeta {          // one slot of the data ring
-    int64_t unit;          // region-relative unit index
-    int32_t tag;           // row descriptor index, -1 = no unit (end of the stream)
-    int32_t pad;
-};
-
-struct WarpRing {
-    uint8_t data[kRing][1 << kUnitShift];
-    UnitMeta meta[kRing];
-    RowDesc rows[kRowRing];
-};
-
-constexpr size_t kRingBytes = sizeof(WarpRing) * kWarps;
-
-__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
-    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gsrc) : "memory");
+__device__ __forceinline__ Vec32 ld_stream32(const void *p) {
+    Vec32 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r.v[0]), "=r"(r.v[1]), "=r"(r.v[2]), "=r"(r.v[3]), "=r"(r.v[4]), "=r"(r.v[5]), "=r"(r.v[6]),
+                   "=r"(r.v[7])
+                 : "l"(p));
+    return r;
 }
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+
+__device__ __forceinline__ uint4 ld_x16(const void *p, bool smem) {
+    uint4 v;
+    if (smem) {
+        v = *reinterpret_cast<const uint4 *>(p);
+    } else {
+        asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    }
+    return v;
 }
 
 __device__ __forceinline__ uint32_t mix_granule(uint64_t g) {
@@ -139,117 +122,81 @@ __device__ __forceinline__ int unit_dom(const GemvArgs &a, uint64_t u) {
     return d ^ a.flip;
 }
 
-// ---- arithmetic: widen to fp32, packed fma.rn.f32x2 --------------------------------------------
-
-__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
-    return (static_cast<unsigned long long>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
-}
-__device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsigned long long x,
-                                                    unsigned long long c) {
-    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(a), "l"(x));
-    return c;
-}
-
-template <int DT> __device__ __forceinline__ unsigned long long widen2(uint32_t v);
-template <> __device__ __forceinline__ unsigned long long widen2<L2D_BF16>(uint32_t v) {
-    return (static_cast<unsigned long long>(v & 0xffff0000u) << 32) | (v << 16);  // exact
-}
-template <> __device__ __forceinline__ unsigned long long widen2<L2D_F16>(uint32_t v) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&v));  // exact
-    return pack2(f.x, f.y);
+// acc += a.lo*x.lo + a.hi*x.hi for packed f16 / bf16 pairs: each product is exact in fp32 and each
+// FMA rounds once, exactly as fmaf on the widened values.
+__device__ __forceinline__ float fma2_f16(uint32_t a, uint32_t x, float acc) {
+    asm("{\n\t.reg .b16 al, ah, xl, xh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {xl, xh}, %2;\n\t"
+        "fma.rn.f32.f16 %0, al, xl, %0;\n\tfma.rn.f32.f16 %0, ah, xh, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(a), "r"(x));
+    return acc;
 }
 
-template <int DT> __device__ __forceinline__ float elem(const uint8_t *p) {
-    if (DT == L2D_F32) return *reinterpret_cast<const float *>(p);
-    const uint16_t h = *reinterpret_cast<const uint16_t *>(p);
-    if (DT == L2D_F16) return __half2float(__ushort_as_half(h));
-    return __uint_as_float(static_cast<uint32_t>(h) << 16);
+__device__ __forceinline__ float fma2_bf16(uint32_t a, uint32_t x, float acc) {
+    asm("{\n\t.reg .b16 al, ah, xl, xh;\n\tmov.b32 {al, ah}, %1;\n\tmov.b32 {xl, xh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, al, xl, %0;\n\tfma.rn.f32.bf16 %0, ah, xh, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(a), "r"(x));
+    return acc;
 }
 
-// Lane accumulators: four packed pairs (eight fp32 partial sums) plus a scalar for edge elements.
-struct Acc {
-    unsigned long long p0, p1, p2, p3;
-    float edge;
-    __device__ __forceinline__ void reset() {
-        p0 = p1 = p2 = p3 = 0ull;
-        edge = 0.f;
+// Packed fp32: (acc.lo, acc.hi) += (a.lo*x.lo, a.hi*x.hi).
+__device__ __forceinline__ unsigned long long fma_f32x2(uint32_t a0, uint32_t a1, uint32_t x0, uint32_t x1,
+                                                        unsigned long long acc) {
+    unsigned long long a = (static_cast<unsigned long long>(a1) << 32) | a0;
+    unsigned long long x = (static_cast<unsigned long long>(x1) << 32) | x0;
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(x));
+    return acc;
+}
+
+// Accumulators of one lane: four independent fp32 chains (fp16/bf16) or two packed pairs (fp32).
+template <int DT> struct Acc;
+
+template <> struct Acc<L2D_F32> {
+    unsigned long long p0 = 0ull, p1 = 0ull;
+    __device__ __forceinline__ void unit(const Vec32 &a, const uint4 &x0, const uint4 &x1) {
+        p0 = fma_f32x2(a.v[0], a.v[1], x0.x, x0.y, p0);
+        p1 = fma_f32x2(a.v[2], a.v[3], x0.z, x0.w, p1);
+        p0 = fma_f32x2(a.v[4], a.v[5], x1.x, x1.y, p0);
+        p1 = fma_f32x2(a.v[6], a.v[7], x1.z, x1.w, p1);
     }
     __device__ __forceinline__ float total() const {
-        const float2 a = *reinterpret_cast<const float2 *>(&p0), b = *reinterpret_cast<const float2 *>(&p1);
-        const float2 c = *reinterpret_cast<const float2 *>(&p2), d = *reinterpret_cast<const float2 *>(&p3);
-        return ((a.x + a.y) + (b.x + b.y)) + ((c.x + c.y) + (d.x + d.y)) + edge;
+        float2 f0 = *reinterpret_cast<const float2 *>(&p0), f1 = *reinterpret_cast<const float2 *>(&p1);
+        return (f0.x + f0.y) + (f1.x + f1.y);
+    }
+    static __device__ __forceinline__ float elem(const uint8_t *p) { return *reinterpret_cast<const float *>(p); }
+    __device__ __forceinline__ void scalar(float a, float x) {
+        float2 f0 = *reinterpret_cast<float2 *>(&p0);
+        f0.x = fmaf(a, x, f0.x);
+        p0 = *reinterpret_cast<unsigned long long *>(&f0);
     }
 };
 
-// Swizzled position of 16-byte chunk Q of a staged fp32 x vector: lane l reads the C chunks
-// 4l/C*... of its unit with C = 2 (fp32 A) or 4 (fp16/bf16 A), so XOR-ing the low bits with
-// (Q >> 3) spreads every 8-lane group over all eight 16-byte bank groups (no bank conflicts).
-template <int C> __device__ __forceinline__ int64_t swz(int64_t q) { return q ^ ((q >> 3) & (C - 1)); }
-
-// One unit (32 bytes of A per lane) times the matching x: `e0` is the row-relative index of the
-// lane's first element.
-template <int DT, bool XS>
-__device__ __forceinline__ void unit_fma(Acc &acc, const uint4 a0, const uint4 a1, const uint8_t *xrow, int64_t e0) {
-    if (XS) {
-        const float4 *xs = reinterpret_cast<const float4 *>(xrow);
-        if (DT == L2D_F32) {
-            const int64_t q = e0 >> 2;  // 8 elements: chunks q, q+1
-            const float4 x0 = xs[swz<2>(q)], x1 = xs[swz<2>(q + 1)];
-            acc.p0 = ffma2(pack2(__uint_as_float(a0.x), __uint_as_float(a0.y)), pack2(x0.x, x0.y), acc.p0);
-            acc.p1 = ffma2(pack2(__uint_as_float(a0.z), __uint_as_float(a0.w)), pack2(x0.z, x0.w), acc.p1);
-            acc.p2 = ffma2(pack2(__uint_as_float(a1.x), __uint_as_float(a1.y)), pack2(x1.x, x1.y), acc.p2);
-            acc.p3 = ffma2(pack2(__uint_as_float(a1.z), __uint_as_float(a1.w)), pack2(x1.z, x1.w), acc.p3);
-        } else {
-            const int64_t q = e0 >> 2;  // 16 elements: chunks q .. q+3
-            const float4 x0 = xs[swz<4>(q)], x1 = xs[swz<4>(q + 1)], x2 = xs[swz<4>(q + 2)], x3 = xs[swz<4>(q + 3)];
-            acc.p0 = ffma2(widen2<DT>(a0.x), pack2(x0.x, x0.y), acc.p0);
-            acc.p1 = ffma2(widen2<DT>(a0.y), pack2(x0.z, x0.w), acc.p1);
-            acc.p2 = ffma2(widen2<DT>(a0.z), pack2(x1.x, x1.y), acc.p2);
-            acc.p3 = ffma2(widen2<DT>(a0.w), pack2(x1.z, x1.w), acc.p3);
-            acc.p0 = ffma2(widen2<DT>(a1.x), pack2(x2.x, x2.y), acc.p0);
-            acc.p1 = ffma2(widen2<DT>(a1.y), pack2(x2.z, x2.w), acc.p1);
-            acc.p2 = ffma2(widen2<DT>(a1.z), pack2(x3.x, x3.y), acc.p2);
-            acc.p3 = ffma2(widen2<DT>(a1.w), pack2(x3.z, x3.w), acc.p3);
-        }
-    } else {
-        constexpr int eb = DT == L2D_F32 ? 4 : 2;
-        const uint8_t *xp = xrow + e0 * eb;
-        uint4 x0, x1;
-        asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(x0.x), "=r"(x0.y), "=r"(x0.z), "=r"(x0.w) : "l"(xp));
-        asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
-            : "=r"(x1.x), "=r"(x1.y), "=r"(x1.z), "=r"(x1.w)
-            : "l"(xp + 16));
-        if (DT == L2D_F32) {
-            acc.p0 = ffma2((static_cast<unsigned long long>(a0.y) << 32) | a0.x,
-                           (static_cast<unsigned long long>(x0.y) << 32) | x0.x, acc.p0);
-            acc.p1 = ffma2((static_cast<unsigned long long>(a0.w) << 32) | a0.z,
-                           (static_cast<unsigned long long>(x0.w) << 32) | x0.z, acc.p1);
-            acc.p2 = ffma2((static_cast<unsigned long long>(a1.y) << 32) | a1.x,
-                           (static_cast<unsigned long long>(x1.y) << 32) | x1.x, acc.p2);
-            acc.p3 = ffma2((static_cast<unsigned long long>(a1.w) << 32) | a1.z,
-                           (static_cast<unsigned long long>(x1.w) << 32) | x1.z, acc.p3);
-        } else {
-            acc.p0 = ffma2(widen2<DT>(a0.x), widen2<DT>(x0.x), acc.p0);
-            acc.p1 = ffma2(widen2<DT>(a0.y), widen2<DT>(x0.y), acc.p1);
-            acc.p2 = ffma2(widen2<DT>(a0.z), widen2<DT>(x0.z), acc.p2);
-            acc.p3 = ffma2(widen2<DT>(a0.w), widen2<DT>(x0.w), acc.p3);
-            acc.p0 = ffma2(widen2<DT>(a1.x), widen2<DT>(x1.x), acc.p0);
-            acc.p1 = ffma2(widen2<DT>(a1.y), widen2<DT>(x1.y), acc.p1);
-            acc.p2 = ffma2(widen2<DT>(a1.z), widen2<DT>(x1.z), acc.p2);
-            acc.p3 = ffma2(widen2<DT>(a1.w), widen2<DT>(x1.w), acc.p3);
-        }
+template <int DT> struct AccHalf {
+    float c0 = 0.f, c1 = 0.f, c2 = 0.f, c3 = 0.f;
+    static __device__ __forceinline__ float f(uint32_t a, uint32_t x, float c) {
+        return DT == L2D_F16 ? fma2_f16(a, x, c) : fma2_bf16(a, x, c);
     }
-}
-
-// x element e of a row (staged fp32, swizzled, or global in the input type).
-template <int DT, bool XS> __device__ __forceinline__ float x_elem(const uint8_t *xrow, int64_t e) {
-    if (XS) {
-        constexpr int C = DT == L2D_F32 ? 2 : 4;
-        return reinterpret_cast<const float *>(xrow)[swz<C>(e >> 2) * 4 + (e & 3)];
+    __device__ __forceinline__ void unit(const Vec32 &a, const uint4 &x0, const uint4 &x1) {
+        c0 = f(a.v[0], x0.x, c0);
+        c1 = f(a.v[1], x0.y, c1);
+        c2 = f(a.v[2], x0.z, c2);
+        c3 = f(a.v[3], x0.w, c3);
+        c0 = f(a.v[4], x1.x, c0);
+        c1 = f(a.v[5], x1.y, c1);
+        c2 = f(a.v[6], x1.z, c2);
+        c3 = f(a.v[7], x1.w, c3);
     }
-    constexpr int eb = DT == L2D_F32 ? 4 : 2;
-    return elem<DT>(xrow + e * eb);
-}
+    __device__ __forceinline__ float total() const { return (c0 + c1) + (c2 + c3); }
+    static __device__ __forceinline__ float elem(const uint8_t *p) {
+        const uint16_t h = *reinterpret_cast<const uint16_t *>(p);
+        if (DT == L2D_F16) return __half2float(__ushort_as_half(h));
+        return __uint_as_float(static_cast<uint32_t>(h) << 16);
+    }
+    __device__ __forceinline__ void scalar(float a, float x) { c0 = fmaf(a, x, c0); }
+};
+template <> struct Acc<L2D_F16> : AccHalf<L2D_F16> {};
+template <> struct Acc<L2D_BF16> : AccHalf<L2D_BF16> {};
 
 template <int DT> __device__ __forceinline__ void store_out(uint8_t *y, float v);
 template <> __device__ __forceinline__ void store_out<L2D_F32>(uint8_t *y, float v) { *reinterpret_cast<float *>(y) = v; }
@@ -260,28 +207,24 @@ template <> __device__ __forceinline__ void store_out<L2D_BF16>(uint8_t *y, floa
     *reinterpret_cast<__nv_bfloat16 *>(y) = __float2bfloat16_rn(v);
 }
 
-// Stages the x vectors of problems [b0, b0 + nb) as fp32, swizzled, x_stride_f32 floats apart.
-template <int DT> __device__ __forceinline__ void stage_x(const GemvArgs &a, float *xs, int64_t b0, int64_t nb) {
-    constexpr int C = DT == L2D_F32 ? 2 : 4;
-    constexpr int eb = DT == L2D_F32 ? 4 : 2;
-    const int64_t chunks = a.x_stride_f32 / 4;
+// Shared-memory staging of the x vectors of problems [b0, b0 + nb): returns the base pointer the
+// row code indexes as xs + (b - b0) * row_bytes.
+__device__ __forceinline__ const uint8_t *stage_x(const GemvArgs &a, uint8_t *smem, int64_t b0, int64_t nb) {
+    const int64_t rb16 = (a.row_bytes + 15) & ~int64_t(15);
     for (int64_t b = 0; b < nb; ++b) {
         const uint8_t *src = a.x + (b0 + b) * a.stride_x_bytes;
-        float4 *dst = reinterpret_cast<float4 *>(xs + b * a.x_stride_f32);
-        for (int64_t q = threadIdx.x; q < chunks; q += blockDim.x) {
-            float v[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int64_t e = 4 * q + k;
-                v[k] = e < a.N ? elem<DT>(src + e * eb) : 0.f;
+        uint8_t *dst = smem + b * rb16;
+        for (int64_t o = threadIdx.x * 16; o < rb16; o += blockDim.x * 16) {
+            if (o + 16 <= a.row_bytes) {
+                *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
+            } else {
+                for (int64_t k = o; k < o + 16; ++k) dst[k] = k < a.row_bytes ? src[k] : 0;
             }
-            dst[swz<C>(q)] = make_float4(v[0], v[1], v[2], v[3]);
         }
     }
     __syncthreads();
+    return smem;
 }
-
-// ---- rows ------------------------------------------------------------------------------------
 
 // Balance between unequal domain groups: a fraction num/den = (n_big - n_small)/(n_big + n_small) of
 // the rows, spread evenly, is taken whole by the bigger group and skipped by the smaller one.  Row r
@@ -315,11 +258,12 @@ struct RowIter {  // rows_total < 2^31 (checked when the call is set up)
 };
 
 // A row whose pair atomic has been issued by lane 0 but whose returned value is not inspected
-// yet; it is resolved at the warp's next publish, so the atomic's round trip overlaps with work.
+// yet.  It is resolved after the warp has issued the next row's first loads, so the atomic's round
+// trip overlaps with memory traffic instead of stalling the warp.
 struct Pending {
     unsigned long long old;
     uint8_t *yp;
-    int32_t row;
+    int64_t row;
     float sum;
     int grp;
     bool active;
@@ -335,20 +279,92 @@ template <int DT_OUT> __device__ __forceinline__ void resolve(const GemvArgs &a,
     }
 }
 
-// Lane 0: the row's result.  A row owned by one group is stored directly.  Otherwise each group adds
-// ~bits(partial) into its own 32-bit half of the row's pair word; ~bits is never 0 for a value
-// arithmetic produces, so the group that finds the other half non-zero holds both partials and
-// finishes the row (in resolve, at this warp's next publish).
-template <int DT_OUT>
-__device__ __forceinline__ void publish(const GemvArgs &a, Pending &pend, int32_t row, int32_t b, int32_t i, int grp,
-                                        bool shared, float sum) {
+// One row of A for one domain group.  SPLIT: the row is shared by both groups (false for the
+// unsplit kernel and for spill rows, which the bigger group takes whole).
+template <int DT_IN, int DT_OUT>
+__device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool SPLIT, int grp, int lane,
+                                         const uint8_t *xs, int64_t xs_b0, Pending &pend) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
-    uint8_t *yp = a.y + (static_cast<int64_t>(b) * a.stride_y_elems + i) * eo;
-    if (!shared) {
+    constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
+    const int64_t row = it.row, b = it.b, i = it.i;
+    const uint8_t *rowp = a.A + b * a.stride_a_bytes + i * a.lda_bytes;
+    const bool xsm = xs != nullptr;
+    const uint8_t *xrow = xsm ? xs + (b - xs_b0) * ((a.row_bytes + 15) & ~int64_t(15)) : a.x + b * a.stride_x_bytes;
+    uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
+    const uint64_t rs = static_cast<uint64_t>(rowp - a.region_base);
+    const uint64_t re = rs + static_cast<uint64_t>(a.row_bytes);
+    const uint64_t u0 = rs >> kUnitShift;
+    const uint64_t u1 = (re + (1u << kUnitShift) - 1) >> kUnitShift;
+    if (u0 == u1) {  // N == 0: y = 0, written once
+        if (lane == 0 && grp == 0) store_out<DT_OUT>(yp, 0.0f);
+        return;
+    }
+    const uint8_t *abase = a.region_base + lane * 32;
+    const int64_t xoff0 = static_cast<int64_t>(lane) * 32 - static_cast<int64_t>(rs);
+    Acc<DT_IN> acc;
+    bool saw_mine = false, saw_other = false, resolved = false;
+    for (uint64_t ub = u0; ub < u1; ub += 64) {
+        const uint64_t ua = ub + lane, uc = ub + 32 + lane;
+        const bool ina = ua < u1, inc = uc < u1;
+        const bool fa = ina && (ua << kUnitShift) >= rs && ((ua + 1) << kUnitShift) <= re;
+        const bool fc = inc && (uc << kUnitShift) >= rs && ((uc + 1) << kUnitShift) <= re;
+        bool ma = ina, mc = inc;
+        if (SPLIT) {
+            ma = ina && unit_dom(a, ua) == grp;
+            mc = inc && unit_dom(a, uc) == grp;
+            saw_other |= __any_sync(0xffffffffu, (ina && !ma) || (inc && !mc));
+        }
+        uint64_t full = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && fa)) |
+                        (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && fc)) << 32);
+        uint64_t edge = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && !fa)) |
+                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && !fc)) << 32);
+        saw_mine |= (full | edge) != 0ull;
+        while (full) {
+            int idx[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                idx[u] = full ? __ffsll(static_cast<long long>(full)) - 1 : -1;
+                full &= full - 1;
+            }
+            Vec32 av[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+                if (idx[u] >= 0) av[u] = ld_stream32(abase + ((ub + idx[u]) << kUnitShift));
+            if (!resolved) {
+                if (lane == 0) resolve<DT_OUT>(a, pend);
+                resolved = true;
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                if (idx[u] >= 0) {
+                    const uint8_t *xp = xrow + static_cast<int64_t>((ub + idx[u]) << kUnitShift) + xoff0;
+                    const uint4 x0 = ld_x16(xp, xsm), x1 = ld_x16(xp + 16, xsm);
+                    acc.unit(av[u], x0, x1);
+                }
+            }
+        }
+        while (edge) {  // units cut by the row's start or end: element by element (rare)
+            const int e = __ffsll(static_cast<long long>(edge)) - 1;
+            edge &= edge - 1;
+            const uint64_t p0 = ((ub + e) << kUnitShift) + lane * 32;
+            const uint64_t lo = p0 > rs ? p0 : rs;
+            const uint64_t hi = p0 + 32 < re ? p0 + 32 : re;
+            for (uint64_t o = lo; o < hi; o += eb)
+                acc.scalar(Acc<DT_IN>::elem(a.region_base + o), Acc<DT_IN>::elem(xrow + (o - rs)));
+        }
+    }
+    float sum = acc.total();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane != 0 || !saw_mine) return;
+    if (!SPLIT || !saw_other) {
         store_out<DT_OUT>(yp, sum);
         return;
     }
-    resolve<DT_OUT>(a, pend);
+    // Both domain groups own part of this row.  Each adds ~bits(partial) into its own 32-bit half
+    // of the row's pair word; ~bits is never 0 for a value arithmetic produces, so the group that
+    // finds the other half non-zero holds both partials and finishes the row (in resolve()).
+    if (!resolved) resolve<DT_OUT>(a, pend);
     pend.old = atomicAdd(a.pair + row, static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp));
     pend.yp = yp;
     pend.row = row;
@@ -356,230 +372,6 @@ __device__ __forceinline__ void publish(const GemvArgs &a, Pending &pend, int32_
     pend.grp = grp;
     pend.active = true;
 }
-
-// The edge units of a row (cut by its start or end, at most two) that this group owns, element by
-// element into acc.edge.
-template <int DT, bool XS>
-__device__ __forceinline__ void row_edges(const GemvArgs &a, Acc &acc, uint64_t rs, const uint8_t *xrow, bool split,
-                                          int grp, int lane) {
-    constexpr int eb = DT == L2D_F32 ? 4 : 2;
-    const uint64_t re = rs + static_cast<uint64_t>(a.row_bytes);
-    const uint64_t ufirst = rs >> kUnitShift, ulast = (re - 1) >> kUnitShift;
-    for (int k = 0; k < 2; ++k) {
-        const uint64_t u = k == 0 ? ufirst : ulast;
-        if (k == 1 && ulast == ufirst) break;
-        const bool full = (u << kUnitShift) >= rs && ((u + 1) << kUnitShift) <= re;
-        if (full || (split && unit_dom(a, u) != grp)) continue;
-        const uint64_t p0 = (u << kUnitShift) + lane * 32;
-        const uint64_t lo = p0 > rs ? p0 : rs, hi = p0 + 32 < re ? p0 + 32 : re;
-        for (uint64_t o = lo; o < hi; o += eb)
-            acc.edge = fmaf(elem<DT>(a.region_base + o), x_elem<DT, XS>(xrow, static_cast<int64_t>((o - rs) / eb)),
-                            acc.edge);
-    }
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// The warp's producer: walks the warp's rows and, within each, the 1 KiB units this group streams
-// (full units of its domain, or every full unit of an unsplit row), 64 units per ballot.
-struct Producer {
-    RowIter it;
-    uint64_t rs, re, ub, uend, mask;
-    int32_t tag, flags, next_tag;
-    bool active, split;
-};
-
-template <int DT, int DT_OUT, bool XS, bool SPLIT>
-struct Pipeline {
-    const GemvArgs &a;
-    WarpRing &W;
-    const float *xs;   // staged x of problem xs_b0 (XS)
-    int64_t xs_b0;
-    int grp, lane, nwarps;
-    int64_t r1;
-    bool small_grp;
-    int32_t step_phase;
-    Producer P;
-    Pending pend;
-
-    __device__ __forceinline__ const uint8_t *xrow_of(int32_t b) const {
-        if (XS) return reinterpret_cast<const uint8_t *>(xs + (b - xs_b0) * a.x_stride_f32);
-        return a.x + static_cast<int64_t>(b) * a.stride_x_bytes;
-    }
-
-    __device__ __forceinline__ void block_mask() {
-        const uint64_t ua = P.ub + lane, uc = P.ub + 32 + lane;
-        const bool ina = ua < P.uend, inc = uc < P.uend;
-        const bool fa = ina && (ua << kUnitShift) >= P.rs && ((ua + 1) << kUnitShift) <= P.re;
-        const bool fc = inc && (uc << kUnitShift) >= P.rs && ((uc + 1) << kUnitShift) <= P.re;
-        bool ma = ina, mc = inc;
-        if (SPLIT && P.split) {
-            ma = ina && unit_dom(a, ua) == grp;
-            mc = inc && unit_dom(a, uc) == grp;
-        }
-        P.mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && fa)) |
-                 (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && fc)) << 32);
-        const bool mine = __any_sync(0xffffffffu, ma || mc);
-        const bool other = __any_sync(0xffffffffu, (ina && !ma) || (inc && !mc));
-        P.flags |= (mine ? 1 : 0) | (other ? 2 : 0);
-    }
-
-    __device__ __forceinline__ void setup_row() {
-        const int64_t off = static_cast<int64_t>(P.it.b) * a.stride_a_bytes + static_cast<int64_t>(P.it.i) * a.lda_bytes;
-        P.rs = static_cast<uint64_t>(a.A + off - a.region_base);
-        P.re = P.rs + static_cast<uint64_t>(a.row_bytes);
-        P.ub = P.rs >> kUnitShift;
-        P.uend = (P.re + (1u << kUnitShift) - 1) >> kUnitShift;
-        P.tag = -1;
-        P.flags = (SPLIT && P.split) ? 4 : 0;
-        P.mask = 0;
-        if (P.ub < P.uend) block_mask();
-    }
-
-    // Moves the producer to its next row (skipping spill rows in the smaller group); false at the end.
-    __device__ __forceinline__ bool next_row(bool first) {
-        for (;;) {
-            if (!first) P.it.advance(a, nwarps, step_phase);
-            first = false;
-            if (P.it.row >= r1) return false;
-            const bool spill = SPLIT && P.it.spill(a);
-            if (spill && small_grp) continue;
-            P.split = SPLIT && !spill;
-            setup_row();
-            return true;
-        }
-    }
-
-    // A row with no full unit of this group: its edge units (if any are ours) finish it here.
-    __device__ __forceinline__ void finish_without_units() {
-        if (a.row_bytes == 0) {  // N == 0: y = 0, written once
-            if (lane == 0 && grp == 0) publish<DT_OUT>(a, pend, P.it.row, P.it.b, P.it.i, grp, false, 0.f);
-            return;
-        }
-        if (!(P.flags & 1)) return;
-        Acc acc;
-        acc.reset();
-        row_edges<DT, XS>(a, acc, P.rs, xrow_of(P.it.b), SPLIT && P.split, grp, lane);
-        const float s = warp_sum(acc.total());
-        if (lane == 0) publish<DT_OUT>(a, pend, P.it.row, P.it.b, P.it.i, grp, (P.flags & 6) == 6, s);
-    }
-
-    // Next unit of the stream into (*unit, *tag); false when the stream is over.
-    __device__ __forceinline__ bool next_unit(uint64_t *unit, int32_t *tag) {
-        for (;;) {
-            if (!P.active) return false;
-            if (P.mask) {
-                const int bit = __ffsll(static_cast<long long>(P.mask)) - 1;
-                P.mask &= P.mask - 1;
-                if (P.tag < 0) {
-                    P.tag = P.next_tag;
-                    P.next_tag = (P.next_tag + 1) & (kRowRing - 1);
-                    if (lane == 0) {
-                        RowDesc &d = W.rows[P.tag];
-                        d.rs = static_cast<int64_t>(P.rs);
-                        d.row = P.it.row;
-                        d.b = P.it.b;
-                        d.i = P.it.i;
-                        d.flags = P.flags;
-                    }
-                }
-                *unit = P.ub + bit;
-                *tag = P.tag;
-                return true;
-            }
-            if (P.ub + 64 < P.uend) {
-                P.ub += 64;
-                block_mask();
-                if (P.tag >= 0 && lane == 0) W.rows[P.tag].flags = P.flags;
-                continue;
-            }
-            if (P.tag >= 0) {
-                if (lane == 0) W.rows[P.tag].flags = P.flags;
-            } else {
-                finish_without_units();
-            }
-            P.active = next_row(false);
-        }
-    }
-
-    // Issues the next unit's two 16-byte async copies into ring slot s (or marks the slot empty);
-    // one commit group per slot keeps the group count aligned with the ring.
-    __device__ __forceinline__ void issue(int s) {
-        uint64_t unit;
-        int32_t tag;
-        if (next_unit(&unit, &tag)) {
-            const uint8_t *src = a.region_base + (unit << kUnitShift) + lane * 32;
-            uint8_t *dst = W.data[s] + lane * 32;
-            cp_async16(dst, src);
-            cp_async16(dst + 16, src + 16);
-            if (lane == 0) {
-                W.meta[s].unit = static_cast<int64_t>(unit);
-                W.meta[s].tag = tag;
-            }
-        } else if (lane == 0) {
-            W.meta[s].tag = -1;
-        }
-        cp_async_commit();
-    }
-
-    __device__ __forceinline__ void flush(int32_t ctag, Acc &acc, uint64_t crs, const uint8_t *cx) {
-        const RowDesc &d = W.rows[ctag];
-        const int32_t flags = d.flags;
-        row_edges<DT, XS>(a, acc, crs, cx, (flags & 4) != 0, grp, lane);
-        const float s = warp_sum(acc.total());
-        if (lane == 0) publish<DT_OUT>(a, pend, d.row, d.b, d.i, grp, (flags & 6) == 6, s);
-    }
-
-    __device__ __forceinline__ void run(int64_t r0) {
-        pend.active = false;
-        P.next_tag = 0;
-        P.active = false;
-        if (r0 + (threadIdx.x >> 5) < r1) {
-            P.it.start(a, static_cast<int32_t>(r0 + (threadIdx.x >> 5)));
-            P.active = next_row(true);
-        }
-        for (int s = 0; s < kRing - 1; ++s) issue(s);
-        int ps = kRing - 1, cs = 0;
-        int32_t ctag = -1;
-        uint64_t crs = 0;
-        const uint8_t *cx = nullptr;
-        Acc acc;
-        acc.reset();
-        for (;;) {
-            issue(ps);
-            ps = ps + 1 == kRing ? 0 : ps + 1;
-            cp_async_wait<kRing - 1>();
-            __syncwarp();
-            const int32_t tag = W.meta[cs].tag;
-            if (tag < 0) break;
-            const int64_t unit = W.meta[cs].unit;
-            if (tag != ctag) {
-                if (ctag >= 0) {
-                    flush(ctag, acc, crs, cx);
-                    acc.reset();
-                }
-                ctag = tag;
-                crs = static_cast<uint64_t>(W.rows[tag].rs);
-                cx = xrow_of(W.rows[tag].b);
-            }
-            const uint4 *sp = reinterpret_cast<const uint4 *>(W.data[cs] + lane * 32);
-            const uint4 a0 = sp[0], a1 = sp[1];
-            constexpr int eb = DT == L2D_F32 ? 4 : 2;
-            const int64_t e0 = (static_cast<int64_t>(unit << kUnitShift) + lane * 32 - static_cast<int64_t>(crs)) / eb;
-            unit_fma<DT, XS>(acc, a0, a1, cx, e0);
-            __syncwarp();
-            cs = cs + 1 == kRing ? 0 : cs + 1;
-        }
-        cp_async_wait<0>();
-        if (ctag >= 0) flush(ctag, acc, crs, cx);
-        if (lane == 0) resolve<DT_OUT>(a, pend);
-        __syncwarp();
-    }
-};
 
 template <int DT_IN, int DT_OUT, bool SPLIT>
 __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem) {
@@ -592,21 +384,27 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     const int64_t r0 = a.rows_total * idx / n_group;
     const int64_t r1 = a.rows_total * (idx + 1) / n_group;
     if (r0 >= r1) return;
-    WarpRing *rings = reinterpret_cast<WarpRing *>(smem);
-    float *xs = reinterpret_cast<float *>(smem + kRingBytes);
-    const int64_t b0 = r0 / a.M;
+    const uint8_t *xs = nullptr;
+    int64_t b0 = 0;
+    if (a.x_smem) {
+        b0 = r0 / a.M;
+        xs = stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
+    }
+    Pending pend;
+    pend.active = false;
+    // The smaller domain group skips the spill rows, which the bigger group takes whole.
+    const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
     const int32_t step_phase =
         a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
-    const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
-    if (a.x_smem) {
-        stage_x<DT_IN>(a, xs, b0, (r1 - 1) / a.M - b0 + 1);
-        Pipeline<DT_IN, DT_OUT, true, SPLIT> p{a, rings[warp], xs, b0, grp, lane, nwarps, r1, small_grp, step_phase};
-        p.run(r0);
-    } else {
-        Pipeline<DT_IN, DT_OUT, false, SPLIT> p{a, rings[warp], xs, b0, grp, lane, nwarps, r1, small_grp, step_phase};
-        p.run(r0);
+    RowIter it;
+    if (r0 + warp < r1) it.start(a, static_cast<int32_t>(r0 + warp));
+    for (int64_t row = r0 + warp; row < r1; row += nwarps, it.advance(a, nwarps, step_phase)) {
+        const bool spill = SPLIT && it.spill(a);
+        if (spill && small_grp) continue;
+        gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
     }
-    __syncthreads();  // the staged x and the rings may be reused for the next slot
+    if (lane == 0) resolve<DT_OUT>(a, pend);
+    if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
 
 __device__ __forceinline__ unsigned long long ld_claim(const unsigned long long *p) {
@@ -633,7 +431,7 @@ __device__ __forceinline__ int warp_claim_any(const GemvArgs &a, unsigned long l
 
 template <int DT_IN, int DT_OUT, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int s_slot;
     __shared__ int s_last;
     __shared__ int s_count;
@@ -729,20 +527,6 @@ int allow_max_smem(KernelFn k, int device) {
     return L2D_OK;
 }
 
-// Shared memory of one launch: the warp rings plus the staged x when it fits (else x is read from
-// global memory and x_stride_f32 is 0).  nb = the most problems any slot's rows can span.
-size_t launch_smem(int64_t N, int64_t nb, int64_t *x_stride_f32) {
-    const int64_t stride = (N + 31) / 32 * 32;
-    const size_t budget = static_cast<size_t>(kSmemLimit) - 8 * 1024;  // static shared memory + margin
-    const size_t xbytes = static_cast<size_t>(stride * 4 * nb);
-    if (N > 0 && kRingBytes + xbytes <= budget) {
-        *x_stride_f32 = stride;
-        return kRingBytes + xbytes;
-    }
-    *x_stride_f32 = 0;
-    return kRingBytes;
-}
-
 // ---------------------------------------------------------------------------------------------
 // Plan
 // ---------------------------------------------------------------------------------------------
@@ -827,8 +611,7 @@ struct l2d_plan {
     int32_t *d_sm_slot = nullptr;
     uint32_t *d_attr_bits = nullptr;
     unsigned long long *d_pair = nullptr;
-    size_t smem_bytes = 0;    // dynamic shared memory of a launch (warp rings + staged x)
-    int64_t x_stride_f32 = 0; // floats between staged x vectors (0 = x read from global memory)
+    size_t x_smem_bytes = 0;  // dynamic shared memory holding the x vectors (0 = read x through L1)
     unsigned long long *d_claim = nullptr;
     unsigned long long *d_ctl = nullptr;
 };
@@ -1027,22 +810,23 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         delete p;
         return set_error(L2D_ERR_CUDA, "plan upload: %s", cudaGetErrorString(e));
     }
-    // Shared memory: the warp rings plus x staged as fp32 when it fits.  Every slot gets at most
-    // R/n_min + 1 contiguous rows, and k contiguous rows touch at most ceil(k / M) + 1 problems.
-    {
+    // x staging: the most problems any slot's rows can span.  Every slot partition (all SMs, one
+    // domain group, or the bigger group with spill rows) gives a slot at most ~2R/n_min + 1
+    // contiguous rows, and k contiguous rows touch at most ceil(k / M) + 1 problems.
+    if (p->rows_total > 0 && d.N > 0) {
         int n_min = p->n_slots;
         if (p->has_domains) n_min = std::min({n_min, p->n_dom[0], p->n_dom[1]});
-        const int64_t max_rows = p->rows_total / std::max(n_min, 1) + 2;
-        const int64_t max_nb = std::min<int64_t>(d.batch, (max_rows + std::max<int64_t>(d.M, 1) - 1) /
-                                                              std::max<int64_t>(d.M, 1) + 1);
-        p->smem_bytes = launch_smem(d.N, max_nb, &p->x_stride_f32);
-        for (bool split : {false, true}) {
-            const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, split), d.device);
-            if (fe != L2D_OK) {
-                cudaFree(p->dev_block);
-                delete p;
-                return fe;
-            }
+        const int64_t max_rows = 2 * p->rows_total / std::max(n_min, 1) + 2;
+        const int64_t max_nb = std::min<int64_t>(d.batch, (max_rows + d.M - 1) / d.M + 1);
+        const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
+        if (max_nb * rb16 <= kXSmemMax) p->x_smem_bytes = static_cast<size_t>(max_nb * rb16);
+    }
+    for (bool split : {false, true}) {
+        const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, split), d.device);
+        if (fe != L2D_OK) {
+            cudaFree(p->dev_block);
+            delete p;
+            return fe;
         }
     }
     *out = p;
@@ -1079,7 +863,6 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     a.x = static_cast<const uint8_t *>(x);
     a.y = static_cast<uint8_t *>(y);
     a.M = p->desc.M;
-    a.N = p->desc.N;
     a.row_bytes = p->desc.N * p->eb_in;
     a.lda_bytes = p->desc.lda * p->eb_in;
     a.stride_a_bytes = p->desc.stride_a * p->eb_in;
@@ -1097,8 +880,7 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     a.n_dom0 = p->n_dom[0];
     a.n_dom1 = p->n_dom[1];
     a.pair = p->d_pair;
-    a.x_smem = p->x_stride_f32 > 0;
-    a.x_stride_f32 = p->x_stride_f32;
+    a.x_smem = p->x_smem_bytes > 0;
     // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes a
     // fraction (n_big - n_small)/(n_big + n_small) of the rows whole, spread evenly, so every SM
     // streams the same bytes.  The swapped control stays pure (no spill rows).
@@ -1115,7 +897,7 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != p->device) cudaSetDevice(p->device);
-    k<<<p->n_slots, kThreads, p->smem_bytes, static_cast<cudaStream_t>(stream)>>>(a);
+    k<<<p->n_slots, kThreads, p->x_smem_bytes, static_cast<cudaStream_t>(stream)>>>(a);
     cudaError_t e = cudaGetLastError();
     if (prev >= 0 && prev != p->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
@@ -1312,7 +1094,6 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
     a.x = static_cast<const uint8_t *>(x);
     a.y = static_cast<uint8_t *>(y);
     a.M = d.M;
-    a.N = d.N;
     a.row_bytes = d.N * eb;
     a.lda_bytes = d.lda * eb;
     a.stride_a_bytes = d.stride_a * eb;
@@ -1339,20 +1120,21 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
         a.spill_num = std::abs(n_dom[1] - n_dom[0]);
         a.spill_den = n_dom[0] + n_dom[1];
     }
-    // Shared memory, sized as l2d_plan_create sizes it.
-    int n_min = num_sm;
-    if (split) n_min = std::min({n_min, n_dom[0], n_dom[1]});
-    const int64_t max_rows = R / std::max(n_min, 1) + 2;
-    const int64_t max_nb = std::min<int64_t>(d.batch, (max_rows + std::max<int64_t>(d.M, 1) - 1) /
-                                                          std::max<int64_t>(d.M, 1) + 1);
-    int64_t x_stride = 0;
-    const size_t smem = launch_smem(d.N, max_nb, &x_stride);
-    a.x_smem = x_stride > 0;
-    a.x_stride_f32 = x_stride;
+    // x staging, sized as l2d_plan_create sizes it.
+    size_t x_smem = 0;
+    if (d.N > 0) {
+        int n_min = num_sm;
+        if (split) n_min = std::min({n_min, n_dom[0], n_dom[1]});
+        const int64_t max_rows = 2 * R / std::max(n_min, 1) + 2;
+        const int64_t max_nb = std::min<int64_t>(d.batch, (max_rows + d.M - 1) / d.M + 1);
+        const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
+        if (max_nb * rb16 <= kXSmemMax) x_smem = static_cast<size_t>(max_nb * rb16);
+    }
+    a.x_smem = x_smem > 0;
     KernelFn k = pick_kernel(d.dtype_in, d.dtype_out, split);
     st = allow_max_smem(k, d.device);
     if (st != L2D_OK) return st;
-    k<<<num_sm, kThreads, smem, cs>>>(a);
+    k<<<num_sm, kThreads, x_smem, cs>>>(a);
     L2D_CUDA_TRY(cudaGetLastError());
     return L2D_OK;
 }
