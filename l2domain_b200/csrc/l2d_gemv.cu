@@ -41,7 +41,8 @@
 namespace l2d {
 
 constexpr int kUnitShift = 10;  // 1 KiB units: 32 bytes per lane
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
+constexpr int kUnroll = 8;      // units in flight per warp
 constexpr int kXSmemMax = 96 * 1024;
 
 struct GemvArgs {
@@ -278,44 +279,92 @@ template <int DT_OUT> __device__ __forceinline__ void resolve(const GemvArgs &a,
     }
 }
 
-// ---- the warp pipeline ------------------------------------------------------------------------
-//
-// A warp streams the units of its rows (every full unit of an unsplit row, the group's own units of
-// a split row) as a sequence of row-pure batches of up to kBatch units, alternating between two
-// register buffers: while one batch is multiplied, the next one is in flight, across row
-// boundaries, so the loads never drain between rows.  Per-row data lives in a 4-entry descriptor
-// ring in shared memory; the accumulator row is finished (edge elements, warp reduction, publish)
-// when a batch of a later row comes up.
-
-constexpr int kBatch = 4;
-
-struct RowDescR {
-    int64_t rs;                 // region-relative byte offset of the row start
-    int32_t row, b, i, flags;   // flags: 1 the group owns units of the row, 2 the other group does,
-                                // 4 the row is split between the groups
-    int32_t pad[2];
-};
-
-struct Batch {
-    Vec32 d[kBatch];
-    uint32_t u[kBatch];  // region-relative unit indices
-    int n;               // valid units, 0 = end of the stream
-    int tag;             // row descriptor
-};
-
-template <int DT_OUT>
-__device__ __forceinline__ void publish(const GemvArgs &a, Pending &pend, int64_t row, int64_t b, int64_t i, int grp,
-                                        bool shared, float sum) {
+// One row of A for one domain group.  SPLIT: the row is shared by both groups (false for the
+// unsplit kernel and for spill rows, which the bigger group takes whole).
+template <int DT_IN, int DT_OUT>
+__device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool SPLIT, int grp, int lane,
+                                         const uint8_t *xs, int64_t xs_b0, Pending &pend) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
+    const int64_t row = it.row, b = it.b, i = it.i;
+    const uint8_t *rowp = a.A + b * a.stride_a_bytes + i * a.lda_bytes;
+    const bool xsm = xs != nullptr;
+    const uint8_t *xrow = xsm ? xs + (b - xs_b0) * ((a.row_bytes + 15) & ~int64_t(15)) : a.x + b * a.stride_x_bytes;
     uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
-    if (!shared) {
+    const uint64_t rs = static_cast<uint64_t>(rowp - a.region_base);
+    const uint64_t re = rs + static_cast<uint64_t>(a.row_bytes);
+    const uint64_t u0 = rs >> kUnitShift;
+    const uint64_t u1 = (re + (1u << kUnitShift) - 1) >> kUnitShift;
+    if (u0 == u1) {  // N == 0: y = 0, written once
+        if (lane == 0 && grp == 0) store_out<DT_OUT>(yp, 0.0f);
+        return;
+    }
+    const uint8_t *abase = a.region_base + lane * 32;
+    const int64_t xoff0 = static_cast<int64_t>(lane) * 32 - static_cast<int64_t>(rs);
+    Acc<DT_IN> acc;
+    bool saw_mine = false, saw_other = false, resolved = false;
+    for (uint64_t ub = u0; ub < u1; ub += 64) {
+        const uint64_t ua = ub + lane, uc = ub + 32 + lane;
+        const bool ina = ua < u1, inc = uc < u1;
+        const bool fa = ina && (ua << kUnitShift) >= rs && ((ua + 1) << kUnitShift) <= re;
+        const bool fc = inc && (uc << kUnitShift) >= rs && ((uc + 1) << kUnitShift) <= re;
+        bool ma = ina, mc = inc;
+        if (SPLIT) {
+            ma = ina && unit_dom(a, ua) == grp;
+            mc = inc && unit_dom(a, uc) == grp;
+            saw_other |= __any_sync(0xffffffffu, (ina && !ma) || (inc && !mc));
+        }
+        uint64_t full = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && fa)) |
+                        (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && fc)) << 32);
+        uint64_t edge = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && !fa)) |
+                              (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && !fc)) << 32);
+        saw_mine |= (full | edge) != 0ull;
+        while (full) {
+            int idx[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                idx[u] = full ? __ffsll(static_cast<long long>(full)) - 1 : -1;
+                full &= full - 1;
+            }
+            Vec32 av[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u)
+                if (idx[u] >= 0) av[u] = ld_stream32(abase + ((ub + idx[u]) << kUnitShift));
+            if (!resolved) {
+                if (lane == 0) resolve<DT_OUT>(a, pend);
+                resolved = true;
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                if (idx[u] >= 0) {
+                    const uint8_t *xp = xrow + static_cast<int64_t>((ub + idx[u]) << kUnitShift) + xoff0;
+                    const uint4 x0 = ld_x16(xp, xsm), x1 = ld_x16(xp + 16, xsm);
+                    acc.unit(av[u], x0, x1);
+                }
+            }
+        }
+        while (edge) {  // units cut by the row's start or end: element by element (rare)
+            const int e = __ffsll(static_cast<long long>(edge)) - 1;
+            edge &= edge - 1;
+            const uint64_t p0 = ((ub + e) << kUnitShift) + lane * 32;
+            const uint64_t lo = p0 > rs ? p0 : rs;
+            const uint64_t hi = p0 + 32 < re ? p0 + 32 : re;
+            for (uint64_t o = lo; o < hi; o += eb)
+                acc.scalar(Acc<DT_IN>::elem(a.region_base + o), Acc<DT_IN>::elem(xrow + (o - rs)));
+        }
+    }
+    float sum = acc.total();
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane != 0 || !saw_mine) return;
+    if (!SPLIT || !saw_other) {
         store_out<DT_OUT>(yp, sum);
         return;
     }
     // Both domain groups own part of this row.  Each adds ~bits(partial) into its own 32-bit half
     // of the row's pair word; ~bits is never 0 for a value arithmetic produces, so the group that
     // finds the other half non-zero holds both partials and finishes the row (in resolve()).
-    resolve<DT_OUT>(a, pend);
+    if (!resolved) resolve<DT_OUT>(a, pend);
     pend.old = atomicAdd(a.pair + row, static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp));
     pend.yp = yp;
     pend.row = row;
@@ -324,217 +373,8 @@ __device__ __forceinline__ void publish(const GemvArgs &a, Pending &pend, int64_
     pend.active = true;
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-template <int DT_IN, int DT_OUT, bool SPLIT_T> struct Roll {
-    const GemvArgs &a;
-    RowDescR *rd;  // this warp's descriptor ring (4 entries)
-    const uint8_t *xs;
-    int64_t xs_b0;
-    int grp, lane, nwarps;
-    int64_t r1;
-    bool small_grp;
-    int32_t step_phase;
-    // producer cursor (warp-uniform)
-    RowIter it;
-    uint64_t rs, re, ub, uend, mask;
-    int32_t flags, tag, next_tag;
-    bool active, split;
-    // consumer
-    Acc<DT_IN> acc;
-    int32_t acc_tag;
-    uint64_t acc_rs;
-    const uint8_t *acc_xrow;
-    Pending pend;
-
-    __device__ __forceinline__ const uint8_t *xrow_of(int64_t b) const {
-        if (xs) return xs + (b - xs_b0) * ((a.row_bytes + 15) & ~int64_t(15));
-        return a.x + b * a.stride_x_bytes;
-    }
-
-    __device__ __forceinline__ void block_mask() {
-        const uint64_t ua = ub + lane, uc = ub + 32 + lane;
-        const bool ina = ua < uend, inc = uc < uend;
-        const bool fa = ina && (ua << kUnitShift) >= rs && ((ua + 1) << kUnitShift) <= re;
-        const bool fc = inc && (uc << kUnitShift) >= rs && ((uc + 1) << kUnitShift) <= re;
-        bool ma = ina, mc = inc;
-        if (SPLIT_T && split) {
-            ma = ina && unit_dom(a, ua) == grp;
-            mc = inc && unit_dom(a, uc) == grp;
-        }
-        mask = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && fa)) |
-               (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && fc)) << 32);
-        const bool mine = __any_sync(0xffffffffu, ma || mc);
-        const bool other = __any_sync(0xffffffffu, (ina && !ma) || (inc && !mc));
-        flags |= (mine ? 1 : 0) | (other ? 2 : 0);
-    }
-
-    __device__ __forceinline__ void setup_row() {
-        const int64_t off = static_cast<int64_t>(it.b) * a.stride_a_bytes + static_cast<int64_t>(it.i) * a.lda_bytes;
-        rs = static_cast<uint64_t>(a.A + off - a.region_base);
-        re = rs + static_cast<uint64_t>(a.row_bytes);
-        ub = rs >> kUnitShift;
-        uend = (re + (1u << kUnitShift) - 1) >> kUnitShift;
-        tag = -1;
-        flags = (SPLIT_T && split) ? 4 : 0;
-        mask = 0;
-        if (ub < uend) block_mask();
-    }
-
-    // Moves the cursor to its next row (the smaller group skips spill rows); false at the end.
-    __device__ __forceinline__ bool next_row(bool first) {
-        for (;;) {
-            if (!first) it.advance(a, nwarps, step_phase);
-            first = false;
-            if (it.row >= r1) return false;
-            const bool spill = SPLIT_T && it.spill(a);
-            if (spill && small_grp) continue;
-            split = SPLIT_T && !spill;
-            setup_row();
-            return true;
-        }
-    }
-
-    // The units of a row cut by its start or end (at most two) that the group owns, element by
-    // element into `ac`.
-    __device__ __forceinline__ void edges(Acc<DT_IN> &ac, uint64_t rs_, const uint8_t *xrow, bool split_) const {
-        constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
-        const uint64_t re_ = rs_ + static_cast<uint64_t>(a.row_bytes);
-        const uint64_t ufirst = rs_ >> kUnitShift, ulast = (re_ - 1) >> kUnitShift;
-        for (int k = 0; k < 2; ++k) {
-            const uint64_t u = k == 0 ? ufirst : ulast;
-            if (k == 1 && ulast == ufirst) break;
-            const bool full = (u << kUnitShift) >= rs_ && ((u + 1) << kUnitShift) <= re_;
-            if (full || (split_ && unit_dom(a, u) != grp)) continue;
-            const uint64_t p0 = (u << kUnitShift) + lane * 32;
-            const uint64_t lo = p0 > rs_ ? p0 : rs_, hi = p0 + 32 < re_ ? p0 + 32 : re_;
-            for (uint64_t o = lo; o < hi; o += eb)
-                ac.scalar(Acc<DT_IN>::elem(a.region_base + o), Acc<DT_IN>::elem(xrow + (o - rs_)));
-        }
-    }
-
-    // A row that produced no full unit: N == 0 (y = 0) or only edge elements of this group.
-    __device__ __forceinline__ void finish_without_units() {
-        if (a.row_bytes == 0) {
-            if (lane == 0 && grp == 0) publish<DT_OUT>(a, pend, it.row, it.b, it.i, grp, false, 0.f);
-            return;
-        }
-        if (!(flags & 1)) return;
-        Acc<DT_IN> ac;
-        edges(ac, rs, xrow_of(it.b), SPLIT_T && split);
-        const float s = warp_sum(ac.total());
-        if (lane == 0) publish<DT_OUT>(a, pend, it.row, it.b, it.i, grp, (flags & 6) == 6, s);
-    }
-
-    // Next row-pure batch of up to kBatch units; issues its loads.
-    __device__ __forceinline__ void fill(Batch &B) {
-        B.n = 0;
-        for (;;) {
-            if (!active) return;
-            if (mask) break;
-            if (ub + 64 < uend) {
-                ub += 64;
-                block_mask();
-                if (tag >= 0 && lane == 0) rd[tag].flags = flags;
-                continue;
-            }
-            if (tag >= 0) {
-                if (lane == 0) rd[tag].flags = flags;
-            } else {
-                finish_without_units();
-            }
-            active = next_row(false);
-        }
-        if (tag < 0) {
-            tag = next_tag;
-            next_tag = (next_tag + 1) & 3;
-            if (lane == 0) {
-                RowDescR &d = rd[tag];
-                d.rs = static_cast<int64_t>(rs);
-                d.row = it.row;
-                d.b = it.b;
-                d.i = it.i;
-                d.flags = flags;
-            }
-        }
-        B.tag = tag;
-        const uint8_t *abase = a.region_base + lane * 32;
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-            if (mask) {
-                const int bit = __ffsll(static_cast<long long>(mask)) - 1;
-                mask &= mask - 1;
-                B.u[j] = static_cast<uint32_t>(ub + bit);
-                B.d[j] = ld_stream32(abase + (static_cast<uint64_t>(B.u[j]) << kUnitShift));
-                B.n = j + 1;
-            }
-        }
-    }
-
-    __device__ __forceinline__ void flush() {
-        const RowDescR d = rd[acc_tag];
-        edges(acc, acc_rs, acc_xrow, (d.flags & 4) != 0);
-        const float s = warp_sum(acc.total());
-        if (lane == 0) publish<DT_OUT>(a, pend, d.row, d.b, d.i, grp, (d.flags & 6) == 6, s);
-    }
-
-    __device__ __forceinline__ void compute(const Batch &B) {
-        __syncwarp();  // descriptors written by lane 0 in fill()
-        if (B.tag != acc_tag) {
-            if (acc_tag >= 0) flush();
-            acc = Acc<DT_IN>();
-            acc_tag = B.tag;
-            acc_rs = static_cast<uint64_t>(rd[B.tag].rs);
-            acc_xrow = xrow_of(rd[B.tag].b);
-        }
-        if (lane == 0) resolve<DT_OUT>(a, pend);  // the previous row's atomic has had a batch to return
-        const bool xsm = xs != nullptr;
-        const int64_t xoff0 = static_cast<int64_t>(lane) * 32 - static_cast<int64_t>(acc_rs);
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-            if (j < B.n) {
-                const uint8_t *xp = acc_xrow + static_cast<int64_t>(static_cast<uint64_t>(B.u[j]) << kUnitShift) + xoff0;
-                const uint4 x0 = ld_x16(xp, xsm), x1 = ld_x16(xp + 16, xsm);
-                acc.unit(B.d[j], x0, x1);
-            }
-        }
-    }
-
-    __device__ __forceinline__ void run(int64_t r0, int warp) {
-        pend.active = false;
-        next_tag = 0;
-        acc_tag = -1;
-        acc_rs = 0;
-        acc_xrow = nullptr;
-        active = false;
-        if (r0 + warp < r1) {
-            it.start(a, static_cast<int32_t>(r0 + warp));
-            active = next_row(true);
-        }
-        Batch B0, B1;
-        fill(B0);
-        fill(B1);
-        for (;;) {
-            if (B0.n == 0) break;
-            compute(B0);
-            fill(B0);
-            if (B1.n == 0) break;
-            compute(B1);
-            fill(B1);
-        }
-        __syncwarp();
-        if (acc_tag >= 0) flush();
-        if (lane == 0) resolve<DT_OUT>(a, pend);
-    }
-};
-
 template <int DT_IN, int DT_OUT, bool SPLIT>
-__device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem,
-                                         RowDescR *rd) {
+__device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem) {
     int grp = 0, idx = slot, n_group = a.n_slots;
     if (SPLIT) {
         grp = slot >= a.n_dom0;
@@ -550,12 +390,20 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
         b0 = r0 / a.M;
         xs = stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
     }
+    Pending pend;
+    pend.active = false;
     // The smaller domain group skips the spill rows, which the bigger group takes whole.
     const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
     const int32_t step_phase =
         a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
-    Roll<DT_IN, DT_OUT, SPLIT> r{a, rd + warp * 4, xs, b0, grp, lane, nwarps, r1, small_grp, step_phase};
-    r.run(r0, warp);
+    RowIter it;
+    if (r0 + warp < r1) it.start(a, static_cast<int32_t>(r0 + warp));
+    for (int64_t row = r0 + warp; row < r1; row += nwarps, it.advance(a, nwarps, step_phase)) {
+        const bool spill = SPLIT && it.spill(a);
+        if (spill && small_grp) continue;
+        gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
+    }
+    if (lane == 0) resolve<DT_OUT>(a, pend);
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
 
@@ -589,7 +437,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     __shared__ int s_count;
     __shared__ int s_list[kMaxSmid];
     __shared__ unsigned long long s_epoch;
-    __shared__ RowDescR s_rows[(kThreads / 32) * 4];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     if (warp == 0) {
         const unsigned long long E = ld_claim(a.ctl) + 1ull;
@@ -611,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         }
     }
     __syncthreads();
-    if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT>(a, s_slot, warp, nwarps, lane, smem, s_rows);
+    if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT>(a, s_slot, warp, nwarps, lane, smem);
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -629,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     const int n_left = s_count;
     if (tid == 0 && n_left) atomicAdd(a.ctl + 2, static_cast<unsigned long long>(n_left));
     for (int k = 0; k < n_left; ++k) {
-        run_slot<DT_IN, DT_OUT, SPLIT>(a, s_list[k], warp, nwarps, lane, smem, s_rows);
+        run_slot<DT_IN, DT_OUT, SPLIT>(a, s_list[k], warp, nwarps, lane, smem);
         __syncthreads();
     }
     if (tid == 0) {
