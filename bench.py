@@ -3,11 +3,15 @@
 
 Workload (default ``cfg5``): the row-sharded fp16 GEMV of the configs -- A is M=131072 x N=16384
 fp16 (4 GiB), A ~ N(0, 0.02), x ~ N(0, 1), fp32 accumulation, fp16 y.  With N GPUs each rank owns
-M/N contiguous rows; one step is: NCCL broadcast of x from rank 0, the domain-aware GEMV of the
-rank's shard, NCCL all-gather of y.  With one GPU the step is the GEMV alone (the whole 4 GiB
-matrix).  Every rank's A is larger than L2 at every N <= 8 (>= 512 MiB), so no flush is needed.
+M/N contiguous rows; one step is: x from rank 0 to every rank, the domain-aware GEMV of the rank's
+shard, the y shards gathered on every rank.  The exchange runs over peer memory inside the GEMV
+launch by default (``--collective p2p``: rank 0 pushes x over NVLink, each rank's last CTA pushes
+its rows to every peer) or as NCCL broadcast + all_gather (``--collective nccl``).  With one GPU
+the step is the GEMV alone (the whole 4 GiB matrix).  Every rank's A is larger than L2 at every
+N <= 8 (>= 512 MiB), so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload cfg5]
+                    [--collective p2p|nccl]
 
 ``--impl reference`` times the reference's CPU GEMV check loop (the oracle restatement of
 applications/gemv/src/gemv_k1024_persistent_subwarp.cu:383-390) on all host cores, over a bounded
@@ -39,7 +43,7 @@ EB = {F32: 4, F16: 2, BF16: 2}
 
 WORKLOADS = {
     "cfg5": dict(M=131072, N=16384, batch=1, dtype=F16, a=(NORMAL, 0.0, 0.02), x=(NORMAL, 0.0, 1.0),
-                 name="row-sharded fp16 GEMV, A 131072x16384 (4 GiB), NCCL broadcast(x) + all_gather(y)"),
+                 name="row-sharded fp16 GEMV, A 131072x16384 (4 GiB), x broadcast + y gather"),
     "cfg3": dict(M=28672, N=8192, batch=1, dtype=BF16, a=(NORMAL, 0.0, 0.02), x=(NORMAL, 0.0, 1.0),
                  name="bf16 LLM-decode GEMV, A 28672x8192 (448 MiB)"),
     "cfg4": dict(M=8192, N=8192, batch=32, dtype=F16, a=(UNIFORM, -0.05, 0.05), x=(NORMAL, 0.0, 1.0),
@@ -54,6 +58,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg5")
+    ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: x push and y gather over peer memory inside the GEMV launch (p2p) or NCCL collectives")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline leg")
     ap.add_argument("--no-aux", action="store_true", help="skip the per-mode and L2-resident side measurements")
     return ap.parse_args()
@@ -269,8 +275,25 @@ def run_ours(args, rank, world, local):
 
     shard = RowShard(M, world, rank)
     assert shard.rows == m_loc and shard.row0 == rank * m_loc
+    pstep = None
+    if world > 1 and args.collective == "p2p":
+        from l2domain_b200.shard import PeerGemvStep, exchange_bytes
+
+        pstep = PeerGemvStep(shard, plan, N, dt, dt, local, lambda b: exchange_bytes(b, device=dev))
+        if rank == 0:  # the step's input x, resident in both parities of rank 0's x buffer
+            for par in (0, 1):
+                pstep.x(par).copy_(x)
+        torch.cuda.synchronize()
 
     def step(mode=L.MODE_AWARE, ev=None):
+        if pstep is not None:
+            if ev is not None:
+                ev[0].record(stream)
+            par = pstep(mode, stream)
+            if ev is not None:
+                ev[1].record(stream)
+            return par
+
         def local():
             if ev is not None:
                 ev[0].record(stream)
@@ -293,8 +316,15 @@ def run_ours(args, rank, world, local):
         return float(t.item())
 
     # Sanity check against a float64 torch dot product on sampled rows (the oracle is not used here).
-    step()
+    ShardedGemvStep(shard, x, y_loc, y_full, lambda: plan.gemv(A, x, y_loc, L.MODE_AWARE, stream))()
     torch.cuda.synchronize()
+    gather_exact = None
+    if pstep is not None:  # the peer-memory gather must equal the NCCL gather bit for bit
+        par = step()
+        torch.cuda.synchronize()
+        gather_exact = bool(torch.equal(pstep.y(par), y_full))
+        if not gather_exact or pstep.status():
+            raise SystemExit(f"rank {rank}: peer-memory step differs from NCCL (status {pstep.status()})")
     tdt = {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}[dt]
     Av = A.view(tdt).view(batch * m_loc, N)
     xv = x.view(tdt)
@@ -404,6 +434,13 @@ def run_ours(args, rank, world, local):
     y_host = torch.empty_like(y_full, device="cpu").pin_memory()
 
     def e2e_step():
+        if pstep is not None:
+            par = pstep.next_parity()
+            if rank == 0:
+                pstep.x(par).copy_(x_host, non_blocking=True)
+            step()
+            y_host.copy_(pstep.y(par), non_blocking=True)
+            return
         if rank == 0:
             x.copy_(x_host, non_blocking=True)
         step()
@@ -428,6 +465,8 @@ def run_ours(args, rank, world, local):
 
     if rank == 0:
         clocks = sampler.summary()
+        exchange = (", peer-memory x push + y gather inside the GEMV launch (CUDA IPC over NVLink)"
+                    if pstep is not None else ", NCCL broadcast(x) + all_gather(y)")
         ratio = None
         if modes_us.get("oblivious") and modes_us.get("aware"):
             ratio = round(modes_us["oblivious"] / modes_us["aware"], 4)
@@ -438,7 +477,7 @@ def run_ours(args, rank, world, local):
             "data": "synthetic: seeded splitmix64 stream, A~N(0,0.02), x~N(0,1) (cfg5 distributions), generated on device",
             "config": {"workload": f"{args.workload}: {W['name']}", "M": M, "N": N, "batch": batch,
                        "dtype_in": DT_NAME[dt], "dtype_out": DT_NAME[dt], "rows_per_gpu": m_loc,
-                       "parallelism": f"row-shard x{world}" + (", NCCL broadcast(x) + all_gather(y)" if world > 1 else ""),
+                       "parallelism": f"row-shard x{world}" + (exchange if world > 1 else ""),
                        "mode": "aware", "l2": f"inputs larger than L2 ({a_bytes / 2**20:.0f} MiB of A per GPU), no flush"},
             "modes_us": modes_us, "aware_speedup_vs_oblivious": ratio, "l2_resident": l2res,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -449,15 +488,18 @@ def run_ours(args, rank, world, local):
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(x.numel()), "d2h_bytes_per_step": int(y_full.numel()),
                     "ms_per_step": round(e2e_ms, 6)},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (3 if pstep is not None else 1),
             "clocks": clocks,
             "plan": {"probe_and_plan_s": round(t_plan, 3), "domain_sms": pstats["domain_sms"],
                      "granule_shift": pstats["granule_shift"], "domain_bytes": pstats["domain_bytes"],
                      "split_rows": pstats["split_rows"], "fallback_slots": fstats["fallback_slots"],
                      "calls": fstats["calls"]},
-            "check": {"rows": 64, "rel_l2_vs_f64": rel},
+            "check": {"rows": 64, "rel_l2_vs_f64": rel, "p2p_gather_equals_nccl": gather_exact},
         }
         print(json.dumps(line), flush=True)
+    if pstep is not None:
+        barrier()
+        pstep.close()
     plan.close()
     if world > 1:
         dist.barrier(device_ids=[local])

@@ -219,6 +219,35 @@ L2D_API int l2d_plan_domain_map(const l2d_plan *plan, int *sm_domain, int cap, i
 L2D_API int l2d_gemv_noalloc(const l2d_gemv_desc *desc, const l2d_domain_map *map, const void *x, void *y,
                              int mode, void *stream);
 
+/* ---- row-sharded GEMV over the GPUs of one node (peer memory; no counterpart in the reference) ----
+ * One process (or one shard object) per GPU.  Rank r owns rows [row0, row0 + rows) of an M_total-row
+ * problem; its plan covers exactly those rows (desc.M = rows, desc.A = its rows of A).  Each rank:
+ *   l2d_shard_create -> l2d_shard_handle (exchange the blobs, e.g. an all_gather of bytes)
+ *   -> l2d_shard_connect(all blobs in rank order) -> per step:
+ *      rank 0 writes x into l2d_shard_buffers(l2d_shard_next_parity()) .x, then every rank calls
+ *      l2d_gemv_sharded; after it (stream-ordered) the gathered y of all M_total rows is in that
+ *      parity's .y buffer on every rank.  Consume it before the step after next on the same stream.
+ * Rank 0 pushes x to the peers over NVLink; each rank's GEMV waits for it, then pushes its y rows to
+ * every peer; a last kernel waits for all peers' rows.  Every wait is bounded by timeout_ms (0 =
+ * 2000 ms); a timeout sets a bit in l2d_shard_status (1: x never arrived, 2: a peer's rows never
+ * arrived) and the kernels return, leaving the context usable.  Peer memory sees plain loads/stores. */
+typedef struct l2d_shard l2d_shard;
+L2D_API int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t row0, int64_t rows,
+                             int64_t N, int dtype_in, int dtype_out, uint32_t timeout_ms, l2d_shard **shard);
+/* Writes this rank's exchange blob (an IPC handle plus layout) into blob; *len = its size.  With
+ * blob == NULL only *len is set. */
+L2D_API int l2d_shard_handle(const l2d_shard *shard, void *blob, size_t cap, size_t *len);
+/* blobs: world blobs of blob_len bytes, in rank order (this rank's own included). */
+L2D_API int l2d_shard_connect(l2d_shard *shard, const void *blobs, size_t blob_len);
+/* This rank's x (N elements of dtype_in) and gathered y (M_total of dtype_out) of one parity. */
+L2D_API int l2d_shard_buffers(const l2d_shard *shard, int parity, void **x, void **y);
+L2D_API int l2d_shard_next_parity(const l2d_shard *shard);
+/* One step on the plan's stream order; *parity (may be NULL) receives the buffers' parity used. */
+L2D_API int l2d_gemv_sharded(l2d_plan *plan, l2d_shard *shard, int mode, void *stream, int *parity);
+/* Synchronizes the device, then reads the timeout bits. */
+L2D_API int l2d_shard_status(l2d_shard *shard, uint32_t *status);
+L2D_API int l2d_shard_destroy(l2d_shard *shard);
+
 /* ---- helpers used by the benchmark and the CLI ---- */
 /* Reference-mode inputs (init_data): A/x from mix32 of the flat index (stream 0 = A, 1 = x). */
 L2D_API int l2d_fill_ref(void *dst, int dtype, uint64_t first, uint64_t n, uint32_t seed, int stream,

@@ -113,6 +113,14 @@ SIGNATURES = {
     "l2d_plan_stats_get": (_i, [_vp, C.POINTER(PlanStats)]),
     "l2d_plan_domain_map": (_i, [_vp, _pi, _i, _pi, _pu32]),
     "l2d_gemv_noalloc": (_i, [C.POINTER(GemvDesc), C.POINTER(DomainMap), _vp, _vp, _i, _vp]),
+    "l2d_shard_create": (_i, [_i, _i, _i, _i64, _i64, _i64, _i64, _i, _i, _u32, C.POINTER(_vp)]),
+    "l2d_shard_handle": (_i, [_vp, _vp, _sz, _psz]),
+    "l2d_shard_connect": (_i, [_vp, _vp, _sz]),
+    "l2d_shard_buffers": (_i, [_vp, _i, C.POINTER(_vp), C.POINTER(_vp)]),
+    "l2d_shard_next_parity": (_i, [_vp]),
+    "l2d_gemv_sharded": (_i, [_vp, _vp, _i, _vp, _pi]),
+    "l2d_shard_status": (_i, [_vp, _pu32]),
+    "l2d_shard_destroy": (_i, [_vp]),
     "l2d_fill_ref": (_i, [_vp, _i, _u64, _u64, _u32, _i, _i, _vp]),
     "l2d_fill_cfg": (_i, [_vp, _i, _u64, _u64, _u64, _u64, _i, C.c_float, C.c_float, _vp]),
     "l2d_l2_flush": (_i, [_i, _vp]),
@@ -343,9 +351,94 @@ class GemvPlan:
             pass
 
 
+class PeerShard:
+    """This rank's part of a row-sharded GEMV whose x broadcast and y gather run over peer memory.
+
+    No counterpart in the reference (it is single-GPU).  ``handle()`` gives the bytes every rank
+    must receive from every other (in rank order) before ``connect(blobs)``; ``step(plan)`` runs one
+    sharded GEMV: rank 0's ``x(parity)`` buffer is the input of the step, every rank's ``y(parity)``
+    buffer holds all ``M_total`` rows after it.  Waits are bounded by ``timeout_ms``; ``status()``
+    returns the timeout bits (1: x never arrived, 2: a peer's rows never arrived).
+    """
+
+    def __init__(self, device: int, rank: int, world: int, M_total: int, row0: int, rows: int, N: int,
+                 dtype_in: int, dtype_out: int, timeout_ms: int = 2000):
+        self._s = C.c_void_p(0)
+        self.device, self.rank, self.world = device, rank, world
+        self.M_total, self.row0, self.rows, self.N = M_total, row0, rows, N
+        self._eb_in, self._eb_out = ELEM_BYTES[dtype_in], ELEM_BYTES[dtype_out]
+        check(lib().l2d_shard_create(device, rank, world, M_total, row0, rows, N, dtype_in, dtype_out, timeout_ms,
+                                     C.byref(self._s)))
+
+    def handle(self) -> bytes:
+        n = C.c_size_t(0)
+        check(lib().l2d_shard_handle(self._s, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        check(lib().l2d_shard_handle(self._s, buf, n.value, C.byref(n)))
+        return buf.raw[: n.value]
+
+    def connect(self, blobs: Sequence[bytes]) -> None:
+        if len(blobs) != self.world or len({len(b) for b in blobs}) != 1:
+            raise ValueError(f"expected {self.world} blobs of one size")
+        joined = b"".join(blobs)
+        check(lib().l2d_shard_connect(self._s, joined, len(blobs[0])))
+
+    def buffers(self, parity: int):
+        x, y = C.c_void_p(0), C.c_void_p(0)
+        check(lib().l2d_shard_buffers(self._s, parity, C.byref(x), C.byref(y)))
+        return int(x.value or 0), int(y.value or 0)
+
+    def x_tensor(self, parity: int):
+        """torch uint8 view of this rank's x buffer of one parity (rank 0 writes the step's x here)."""
+        return device_view(self.buffers(parity)[0], self.N * self._eb_in, self.device)
+
+    def y_tensor(self, parity: int):
+        """torch uint8 view of this rank's gathered y buffer (all M_total rows) of one parity."""
+        return device_view(self.buffers(parity)[1], self.M_total * self._eb_out, self.device)
+
+    def next_parity(self) -> int:
+        return int(lib().l2d_shard_next_parity(self._s))
+
+    def step(self, plan: "GemvPlan", mode: int = MODE_AWARE, stream=None) -> int:
+        par = C.c_int(0)
+        check(lib().l2d_gemv_sharded(plan._plan, self._s, mode, _stream_handle(stream), C.byref(par)))
+        return par.value
+
+    def status(self) -> int:
+        v = C.c_uint32(0)
+        check(lib().l2d_shard_status(self._s, C.byref(v)))
+        return int(v.value)
+
+    def close(self) -> None:
+        if self._s and self._s.value:
+            check(lib().l2d_shard_destroy(self._s))
+            self._s = C.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 # --------------------------------------------------------------------------------------------
 # Helpers
 # --------------------------------------------------------------------------------------------
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ holder, so torch can view library-owned device memory."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(ptr: int, nbytes: int, device: int = 0):
+    """A torch uint8 tensor sharing ``nbytes`` of device memory at ``ptr`` (no copy, not owned)."""
+    import torch
+
+    return torch.as_tensor(_CudaArray(ptr, nbytes), device=torch.device("cuda", device))
+
 
 def fill_ref(dst, dtype: int, n: int, seed: int, stream_id: int, integer_mode: bool = False, first: int = 0,
              stream=None) -> None:

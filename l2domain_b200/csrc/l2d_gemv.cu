@@ -71,6 +71,17 @@ struct GemvArgs {
     int64_t spill_den;            // (spill rows are taken whole by big_grp; num = 0: no spill rows)
     int big_grp;                  // the group with more SMs
     unsigned long long *pair;     // [rows_total] packed partial pair, zero between calls
+    // Peer-memory row sharding (shard_world > 1): wait for x from rank 0, push the y shard to peers.
+    int shard_world;
+    int shard_rank;
+    unsigned long long shard_epoch;
+    const unsigned long long *x_flag;  // this rank's x-arrival word (set by rank 0), ranks != 0 wait on it
+    uint8_t *const *peer_y;            // [world] base of each rank's gathered y buffer (this step's parity)
+    unsigned long long *const *peer_flags;  // [world] each rank's flag words; [1 + r] = rank r's y arrived
+    int64_t y_shard_off;               // byte offset of this rank's rows in the gathered y
+    int64_t y_shard_bytes;
+    uint32_t *shard_status;            // bit 0: x wait timed out
+    uint64_t shard_timeout_ns;
     unsigned long long *claim;    // [n_slots] epoch of the last claim
     unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims
 };
@@ -403,8 +414,59 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
         if (spill && small_grp) continue;
         gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
     }
-    if (lane == 0) resolve<DT_OUT>(a, pend);
+    if (lane == 0) {
+        resolve<DT_OUT>(a, pend);
+        __threadfence();  // this warp's y stores are visible before the CTA reports done
+    }
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Sharded prologue: ranks other than 0 wait (bounded) until rank 0 has pushed this step's x.
+__device__ __forceinline__ void shard_wait_x(const GemvArgs &a) {
+    if (a.shard_world <= 1 || a.shard_rank == 0) return;
+    const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
+    while (ld_acquire_sys(a.x_flag) < a.shard_epoch) {
+        if (dev::globaltimer_ns() > deadline) {
+            atomicOr(a.shard_status, 1u);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
+// Sharded epilogue (last CTA): copy this rank's finished y rows into every peer's gathered y, then
+// publish the step's epoch in each peer's flag word for this rank (system-scope release).  The rows
+// start at any element offset; all gathered buffers share one layout, so source and destination
+// have the same alignment: a byte head, 16-byte body, byte tail.  Loads bypass L1 (__ldcg), since
+// the rows were written by other CTAs.
+__device__ __forceinline__ void shard_push_y(const GemvArgs &a) {
+    if (a.shard_world <= 1) return;
+    const uint8_t *src = a.peer_y[a.shard_rank] + a.y_shard_off;
+    const int64_t bytes = a.y_shard_bytes;
+    const int64_t head = min(static_cast<int64_t>((16 - (a.y_shard_off & 15)) & 15), bytes);
+    const int64_t n16 = (bytes - head) / 16;
+    const int64_t tail = head + n16 * 16;
+    for (int p = 0; p < a.shard_world; ++p) {
+        if (p == a.shard_rank) continue;
+        uint8_t *dst = a.peer_y[p] + a.y_shard_off;
+        if (threadIdx.x < head) dst[threadIdx.x] = __ldcg(src + threadIdx.x);
+        for (int64_t k = threadIdx.x; k < n16; k += blockDim.x)
+            reinterpret_cast<uint4 *>(dst + head)[k] = __ldcg(reinterpret_cast<const uint4 *>(src + head) + k);
+        for (int64_t k = tail + threadIdx.x; k < bytes; k += blockDim.x) dst[k] = __ldcg(src + k);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < a.shard_world) st_release_sys(a.peer_flags[threadIdx.x] + 1 + a.shard_rank, a.shard_epoch);
 }
 
 __device__ __forceinline__ unsigned long long ld_claim(const unsigned long long *p) {
@@ -455,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
             s_slot = got;
             s_epoch = E;
             s_count = 0;
+            shard_wait_x(a);
         }
     }
     __syncthreads();
@@ -464,6 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         __threadfence();
         const unsigned long long done = atomicAdd(a.ctl + 1, 1ull);
         s_last = done == gridDim.x - 1;
+        if (s_last) __threadfence();  // acquire side: the other CTAs' y rows before the epilogue
     }
     __syncthreads();
     if (!s_last) return;
@@ -479,6 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         run_slot<DT_IN, DT_OUT, SPLIT>(a, s_list[k], warp, nwarps, lane, smem);
         __syncthreads();
     }
+    shard_push_y(a);
     if (tid == 0) {
         a.ctl[1] = 0ull;
         __threadfence();
@@ -846,11 +911,15 @@ int l2d_plan_destroy(l2d_plan *p) {
     return L2D_OK;
 }
 
-int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void *stream) {
+}  // extern "C"
+
+namespace l2d {
+
+// Kernel arguments of one call on plan p (no sharding); *split tells which kernel variant runs.
+int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, GemvArgs *out, bool *split_out) {
     if (!p) return set_error(L2D_ERR_INVALID, "null plan");
     if (A != p->desc.A) return set_error(L2D_ERR_INVALID, "A differs from the planned allocation");
     if (mode < L2D_MODE_OBLIVIOUS || mode > L2D_MODE_STREAM) return set_error(L2D_ERR_INVALID, "bad mode %d", mode);
-    if (p->rows_total == 0) return L2D_OK;
     if (!x || !y) return set_error(L2D_ERR_INVALID, "null x or y");
     if (reinterpret_cast<uintptr_t>(x) & 15) return set_error(L2D_ERR_UNSUPPORTED, "x must be 16-byte aligned");
     if (reinterpret_cast<uintptr_t>(y) & (p->eb_out - 1)) return set_error(L2D_ERR_INVALID, "y is misaligned");
@@ -859,6 +928,7 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     if (split && !p->has_domains)
         return set_error(L2D_ERR_UNSUPPORTED, "plan has no domain map: only L2D_MODE_STREAM is available");
     GemvArgs a;
+    std::memset(&a, 0, sizeof a);
     a.A = static_cast<const uint8_t *>(A);
     a.x = static_cast<const uint8_t *>(x);
     a.y = static_cast<uint8_t *>(y);
@@ -891,8 +961,12 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
         a.spill_num = std::abs(p->n_dom[1] - p->n_dom[0]);
         a.spill_den = p->n_dom[0] + p->n_dom[1];
     }
-    a.claim = p->d_claim;
-    a.ctl = p->d_ctl;
+    *out = a;
+    *split_out = split;
+    return L2D_OK;
+}
+
+int launch_args(l2d_plan *p, const GemvArgs &a, bool split, void *stream) {
     KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split);
     int prev = -1;
     cudaGetDevice(&prev);
@@ -902,6 +976,45 @@ int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void 
     if (prev >= 0 && prev != p->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
     return L2D_OK;
+}
+
+int plan_device(const l2d_plan *p) { return p->device; }
+int64_t plan_rows(const l2d_plan *p) { return p->rows_total; }
+const l2d_gemv_desc &plan_desc(const l2d_plan *p) { return p->desc; }
+int plan_out_bytes(const l2d_plan *p) { return p->eb_out; }
+size_t gemv_args_size() { return sizeof(GemvArgs); }
+
+// Adds the peer-memory sharding fields to arguments made by build_args.
+int shard_fill_args(GemvArgs *a, int world, int rank, unsigned long long epoch, const unsigned long long *x_flag,
+                    uint8_t *const *peer_y, unsigned long long *const *peer_flags, int64_t y_off, int64_t y_bytes,
+                    uint32_t *status, uint64_t timeout_ns) {
+    a->shard_world = world;
+    a->shard_rank = rank;
+    a->shard_epoch = epoch;
+    a->x_flag = x_flag;
+    a->peer_y = peer_y;
+    a->peer_flags = peer_flags;
+    a->y_shard_off = y_off;
+    a->y_shard_bytes = y_bytes;
+    a->shard_status = status;
+    a->shard_timeout_ns = timeout_ns;
+    return L2D_OK;
+}
+
+}  // namespace l2d
+
+extern "C" {
+
+int l2d_gemv(l2d_plan *p, const void *A, const void *x, void *y, int mode, void *stream) {
+    if (!p) return set_error(L2D_ERR_INVALID, "null plan");
+    if (A != p->desc.A) return set_error(L2D_ERR_INVALID, "A differs from the planned allocation");
+    if (mode < L2D_MODE_OBLIVIOUS || mode > L2D_MODE_STREAM) return set_error(L2D_ERR_INVALID, "bad mode %d", mode);
+    if (p->rows_total == 0) return L2D_OK;
+    GemvArgs a;
+    bool split = false;
+    int st = build_args(p, A, x, y, mode, &a, &split);
+    if (st != L2D_OK) return st;
+    return launch_args(p, a, split, stream);
 }
 
 int l2d_plan_stats_get(l2d_plan *p, l2d_plan_stats *s) {

@@ -100,3 +100,32 @@ def test_dead_rank_surfaces_as_error():
         if p.is_alive():
             p.kill()
     assert got != "no error"
+
+
+def _exchange_worker(rank, world, port, q):
+    """Each rank contributes a distinct blob; every rank must get all of them in rank order."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from l2domain_b200.shard import exchange_bytes
+
+    blob = bytes((rank * 37 + k) % 256 for k in range(96))
+    q.put((rank, exchange_bytes(blob)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_handle_exchange_keeps_rank_order():
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    want = [bytes((r * 37 + k) % 256 for k in range(96)) for r in range(world)]
+    for r in range(world):
+        assert results[r] == want
