@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--collective", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: x push and y gather over peer memory inside the GEMV launch (p2p) or NCCL collectives")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline leg")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override M (a smaller case of the same row shape, for ncu captures)")
     ap.add_argument("--no-aux", action="store_true", help="skip the per-mode and L2-resident side measurements")
     return ap.parse_args()
 
@@ -243,6 +245,8 @@ def run_ours(args, rank, world, local):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     W = WORKLOADS[args.workload]
     M, N, batch, dt = W["M"], W["N"], W["batch"], W["dtype"]
+    if args.rows:
+        M = args.rows
     if batch != 1 and world > 1:
         raise SystemExit("batched workloads run on one GPU")
     if M % world:

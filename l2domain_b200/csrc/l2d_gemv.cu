@@ -950,6 +950,8 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.n_dom0 = p->n_dom[0];
     a.n_dom1 = p->n_dom[1];
     a.pair = p->d_pair;
+    a.claim = p->d_claim;
+    a.ctl = p->d_ctl;
     a.x_smem = p->x_smem_bytes > 0;
     // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes a
     // fraction (n_big - n_small)/(n_big + n_small) of the rows whole, spread evenly, so every SM
@@ -966,7 +968,20 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     return L2D_OK;
 }
 
+// Host-side guard before a launch: every pointer the kernel dereferences unconditionally must be set
+// (a call that reaches the kernel with a missing scratch pointer is refused, never launched).
+int check_args(const GemvArgs &a) {
+    if (!a.x || !a.y || !a.sm_slot || !a.pair || !a.claim || !a.ctl || a.n_slots <= 0 ||
+        (a.row_bytes > 0 && (!a.A || !a.region_base)))
+        return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
+    if (a.shard_world > 1 && (!a.x_flag || !a.peer_y || !a.peer_flags || !a.shard_status))
+        return set_error(L2D_ERR_INVALID, "sharded gemv arguments incomplete (internal error)");
+    return L2D_OK;
+}
+
 int launch_args(l2d_plan *p, const GemvArgs &a, bool split, void *stream) {
+    const int chk = check_args(a);
+    if (chk != L2D_OK) return chk;
     KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split);
     int prev = -1;
     cudaGetDevice(&prev);
@@ -1203,6 +1218,7 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
                                  cudaMemcpyHostToDevice, cs));
 
     GemvArgs a;
+    std::memset(&a, 0, sizeof a);
     a.A = static_cast<const uint8_t *>(d.A);
     a.x = static_cast<const uint8_t *>(x);
     a.y = static_cast<uint8_t *>(y);
@@ -1246,6 +1262,8 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
     a.x_smem = x_smem > 0;
     KernelFn k = pick_kernel(d.dtype_in, d.dtype_out, split);
     st = allow_max_smem(k, d.device);
+    if (st != L2D_OK) return st;
+    st = check_args(a);
     if (st != L2D_OK) return st;
     k<<<num_sm, kThreads, x_smem, cs>>>(a);
     L2D_CUDA_TRY(cudaGetLastError());
