@@ -492,7 +492,7 @@ def run_ours(args, rank, world, local):
             "e2e": {"value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": int(x.numel()), "d2h_bytes_per_step": int(y_full.numel()),
                     "ms_per_step": round(e2e_ms, 6)},
-            "gpu_launches": args.steps * (3 if pstep is not None else 1),
+            "gpu_launches": args.steps,
             "clocks": clocks,
             "plan": {"probe_and_plan_s": round(t_plan, 3), "domain_sms": pstats["domain_sms"],
                      "granule_shift": pstats["granule_shift"], "domain_bytes": pstats["domain_bytes"],

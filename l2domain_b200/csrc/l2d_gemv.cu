@@ -71,16 +71,24 @@ struct GemvArgs {
     int64_t spill_den;            // (spill rows are taken whole by big_grp; num = 0: no spill rows)
     int big_grp;                  // the group with more SMs
     unsigned long long *pair;     // [rows_total] packed partial pair, zero between calls
-    // Peer-memory row sharding (shard_world > 1): wait for x from rank 0, push the y shard to peers.
+    // Peer-memory row sharding (shard_world > 1; batch 1).  Rank 0's first x_slices CTAs push one
+    // slice of x each to every peer; the other ranks' CTAs wait for all slices.  Every final y store
+    // counts its row in a chunk counter; the warp that completes a chunk of 2^chunk_shift rows
+    // pushes it to every peer.  The last CTA waits for every peer's chunks of this step.
     int shard_world;
     int shard_rank;
-    unsigned long long shard_epoch;
-    const unsigned long long *x_flag;  // this rank's x-arrival word (set by rank 0), ranks != 0 wait on it
-    uint8_t *const *peer_y;            // [world] base of each rank's gathered y buffer (this step's parity)
-    unsigned long long *const *peer_flags;  // [world] each rank's flag words; [1 + r] = rank r's y arrived
-    int64_t y_shard_off;               // byte offset of this rank's rows in the gathered y
-    int64_t y_shard_bytes;
-    uint32_t *shard_status;            // bit 0: x wait timed out
+    unsigned long long shard_epoch;     // step number (1, 2, ...): arrival targets are multiples of it
+    unsigned long long *arrive;         // this rank's arrival counters: [0] x slices, [1 + r] chunks of rank r
+    unsigned long long *const *peer_arrive;  // [world] each rank's arrival counters
+    uint8_t *const *peer_x;             // [world] each rank's x buffer of this step's parity
+    uint8_t *const *peer_y;             // [world] each rank's gathered y buffer of this step's parity
+    const unsigned long long *chunks_of;  // [world] chunk count of each rank's rows
+    unsigned long long *chunk_cnt;      // [chunks of this rank] final-row counters (this rank only)
+    int64_t y_shard_off;                // byte offset of this rank's rows in the gathered y
+    int64_t x_bytes;
+    int chunk_shift;
+    int x_slices;
+    uint32_t *shard_status;             // bit 0: x never arrived, bit 1: a peer's rows never arrived
     uint64_t shard_timeout_ns;
     unsigned long long *claim;    // [n_slots] epoch of the last claim
     unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims
@@ -280,19 +288,94 @@ struct Pending {
     bool active;
 };
 
-template <int DT_OUT> __device__ __forceinline__ void resolve(const GemvArgs &a, Pending &p) {
-    if (!p.active) return;
+// Sharded bookkeeping of each warp, kept in shared memory (the unit loop has no registers to spare):
+// [0], [1] chunks the warp completed and still has to push (-1 = none); [2] resolve() stored row
+// `Pending::row` inside the unit loop, to be counted once the loop is done.
+__shared__ int s_shard_warp[kThreads / 32][3];
+
+__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Sharded: copies chunk c of this rank's y rows into every peer's gathered y, then counts it in
+// each peer's arrival counter for this rank.  Called by `nthr` threads with ids 0..nthr-1 (a warp,
+// or a single thread); all gathered buffers share one layout, so source and destination have the
+// same alignment.  The rows were stored by other warps, which fenced before counting them: the
+// caller saw the count complete, so a fence here and L2 loads (__ldcg) read the final values.
+template <int DT_OUT> __device__ void push_chunk(const GemvArgs &a, int c, int t, int nthr) {
+    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    __threadfence();
+    const int64_t r0 = static_cast<int64_t>(c) << a.chunk_shift;
+    const int64_t rows = min(static_cast<int64_t>(1) << a.chunk_shift, a.rows_total - r0);
+    const int64_t off = a.y_shard_off + r0 * eo, bytes = rows * eo;
+    const uint8_t *src = a.peer_y[a.shard_rank] + off;
+    const bool v16 = ((off | bytes) & 15) == 0;
+    for (int p = 0; p < a.shard_world; ++p) {
+        if (p == a.shard_rank) continue;
+        uint8_t *dst = a.peer_y[p] + off;
+        if (v16) {
+            for (int64_t k = t; k < bytes / 16; k += nthr)
+                reinterpret_cast<uint4 *>(dst)[k] = __ldcg(reinterpret_cast<const uint4 *>(src) + k);
+        } else {
+            for (int64_t k = t; k < rows; k += nthr) {
+                if (eo == 4) {
+                    reinterpret_cast<uint32_t *>(dst)[k] = __ldcg(reinterpret_cast<const unsigned int *>(src) + k);
+                } else {
+                    reinterpret_cast<uint16_t *>(dst)[k] = __ldcg(reinterpret_cast<const unsigned short *>(src) + k);
+                }
+            }
+        }
+    }
+    __threadfence_system();
+    if (nthr > 1) __syncwarp();
+    for (int p = t; p < a.shard_world; p += nthr)
+        if (p != a.shard_rank) red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, 1ull);
+}
+
+// Sharded, one thread (lane 0) after a final y store of `row`: counts the row in its chunk and, if
+// it completed the chunk, hands the chunk to the warp (pend.push).  A warp stores at most two final
+// rows between two flush points (the previous row's deferred one and its own), so two slots do.
+template <int DT_OUT, bool SH> __device__ __forceinline__ void count_row(const GemvArgs &a, int64_t row, Pending &pend) {
+    if (!SH) return;
+    const int c = static_cast<int>(row >> a.chunk_shift);
+    const int64_t r0 = static_cast<int64_t>(c) << a.chunk_shift;
+    const int64_t rows = min(static_cast<int64_t>(1) << a.chunk_shift, a.rows_total - r0);
+    __threadfence();  // the y store before its count
+    const unsigned long long old = atomicAdd(a.chunk_cnt + c, 1ull);
+    if (old + 1ull != a.shard_epoch * static_cast<unsigned long long>(rows)) return;
+    int *w = s_shard_warp[threadIdx.x >> 5];
+    w[w[0] < 0 ? 0 : 1] = c;
+}
+
+// Warp-uniform point: push the chunks lane 0 completed, if any, with the whole warp.
+template <int DT_OUT, bool SH> __device__ __forceinline__ void flush_push(const GemvArgs &a, Pending &pend, int lane) {
+    if (!SH) return;
+    int *w = s_shard_warp[threadIdx.x >> 5];
+    __syncwarp();
+    const int c0 = w[0], c1 = w[1];
+    if (c0 < 0) return;
+    push_chunk<DT_OUT>(a, c0, lane, 32);
+    if (c1 >= 0) push_chunk<DT_OUT>(a, c1, lane, 32);
+    __syncwarp();
+    if (lane == 0) w[0] = w[1] = -1;
+}
+
+// Returns true when it stored the final y of row p.row.
+template <int DT_OUT> __device__ __forceinline__ bool resolve(const GemvArgs &a, Pending &p) {
+    if (!p.active) return false;
     p.active = false;
     const uint32_t other = static_cast<uint32_t>(p.old >> (32 * (p.grp ^ 1)));
     if (other != 0u) {
         store_out<DT_OUT>(p.yp, p.sum + __uint_as_float(~other));  // commutative: same bits either way
         a.pair[p.row] = 0ull;
+        return true;
     }
+    return false;
 }
 
 // One row of A for one domain group.  SPLIT: the row is shared by both groups (false for the
 // unsplit kernel and for spill rows, which the bigger group takes whole).
-template <int DT_IN, int DT_OUT>
+template <int DT_IN, int DT_OUT, bool SH>
 __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool SPLIT, int grp, int lane,
                                          const uint8_t *xs, int64_t xs_b0, Pending &pend) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
@@ -307,7 +390,10 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     const uint64_t u0 = rs >> kUnitShift;
     const uint64_t u1 = (re + (1u << kUnitShift) - 1) >> kUnitShift;
     if (u0 == u1) {  // N == 0: y = 0, written once
-        if (lane == 0 && grp == 0) store_out<DT_OUT>(yp, 0.0f);
+        if (lane == 0 && grp == 0) {
+            store_out<DT_OUT>(yp, 0.0f);
+            count_row<DT_OUT, SH>(a, row, pend);
+        }
         return;
     }
     const uint8_t *abase = a.region_base + lane * 32;
@@ -342,7 +428,7 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
             for (int u = 0; u < kUnroll; ++u)
                 if (idx[u] >= 0) av[u] = ld_stream32(abase + ((ub + idx[u]) << kUnitShift));
             if (!resolved) {
-                if (lane == 0) resolve<DT_OUT>(a, pend);
+                if (lane == 0 && resolve<DT_OUT>(a, pend) && SH) s_shard_warp[threadIdx.x >> 5][2] = 1;
                 resolved = true;
             }
 #pragma unroll
@@ -367,15 +453,21 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     float sum = acc.total();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane != 0 || !saw_mine) return;
+    if (lane != 0) return;
+    if (SH && s_shard_warp[threadIdx.x >> 5][2]) {  // the previous row, finished in the loop
+        s_shard_warp[threadIdx.x >> 5][2] = 0;
+        count_row<DT_OUT, SH>(a, pend.row, pend);
+    }
+    if (!saw_mine) return;
     if (!SPLIT || !saw_other) {
         store_out<DT_OUT>(yp, sum);
+        count_row<DT_OUT, SH>(a, row, pend);
         return;
     }
     // Both domain groups own part of this row.  Each adds ~bits(partial) into its own 32-bit half
     // of the row's pair word; ~bits is never 0 for a value arithmetic produces, so the group that
     // finds the other half non-zero holds both partials and finishes the row (in resolve()).
-    if (!resolved) resolve<DT_OUT>(a, pend);
+    if (!resolved && resolve<DT_OUT>(a, pend)) count_row<DT_OUT, SH>(a, pend.row, pend);
     pend.old = atomicAdd(a.pair + row, static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp));
     pend.yp = yp;
     pend.row = row;
@@ -384,7 +476,7 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     pend.active = true;
 }
 
-template <int DT_IN, int DT_OUT, bool SPLIT>
+template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
 __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem) {
     int grp = 0, idx = slot, n_group = a.n_slots;
     if (SPLIT) {
@@ -403,6 +495,11 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     }
     Pending pend;
     pend.active = false;
+    if (SH && lane == 0) {
+        int *w = s_shard_warp[warp];
+        w[0] = w[1] = -1;
+        w[2] = 0;
+    }
     // The smaller domain group skips the spill rows, which the bigger group takes whole.
     const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
     const int32_t step_phase =
@@ -412,12 +509,14 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     for (int64_t row = r0 + warp; row < r1; row += nwarps, it.advance(a, nwarps, step_phase)) {
         const bool spill = SPLIT && it.spill(a);
         if (spill && small_grp) continue;
-        gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
+        gemv_row<DT_IN, DT_OUT, SH>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
+        flush_push<DT_OUT, SH>(a, pend, lane);
     }
     if (lane == 0) {
-        resolve<DT_OUT>(a, pend);
+        if (resolve<DT_OUT>(a, pend)) count_row<DT_OUT, SH>(a, pend.row, pend);
         __threadfence();  // this warp's y stores are visible before the CTA reports done
     }
+    flush_push<DT_OUT, SH>(a, pend, lane);
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
 
@@ -427,46 +526,56 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// Sharded prologue: ranks other than 0 wait (bounded) until rank 0 has pushed this step's x.
-__device__ __forceinline__ void shard_wait_x(const GemvArgs &a) {
-    if (a.shard_world <= 1 || a.shard_rank == 0) return;
-    const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
-    while (ld_acquire_sys(a.x_flag) < a.shard_epoch) {
-        if (dev::globaltimer_ns() > deadline) {
-            atomicOr(a.shard_status, 1u);
-            return;
+// Sharded prologue, one warp per CTA.  Rank 0: CTA i < x_slices pushes slice i of x to every peer
+// and counts it there.  Other ranks: wait (bounded) until all slices of this step have arrived.
+template <bool SH> __device__ __forceinline__ void shard_prologue(const GemvArgs &a, int lane) {
+    if (!SH) return;
+    if (a.shard_rank == 0) {
+        if (static_cast<int>(blockIdx.x) >= a.x_slices) return;
+        const int64_t n16 = a.x_bytes / 16;
+        const int64_t lo = n16 * blockIdx.x / a.x_slices, hi = n16 * (blockIdx.x + 1) / a.x_slices;
+        const bool tail = static_cast<int>(blockIdx.x) == a.x_slices - 1;
+        for (int p = 1; p < a.shard_world; ++p) {
+            for (int64_t k = lo + lane; k < hi; k += 32)
+                reinterpret_cast<uint4 *>(a.peer_x[p])[k] = reinterpret_cast<const uint4 *>(a.x)[k];
+            if (tail)
+                for (int64_t k = n16 * 16 + lane; k < a.x_bytes; k += 32) a.peer_x[p][k] = a.x[k];
         }
-        __nanosleep(200);
+        __threadfence_system();
+        __syncwarp();
+        if (lane >= 1 && lane < a.shard_world) red_release_sys_add(a.peer_arrive[lane], 1ull);
+        return;
     }
+    if (lane == 0) {
+        const unsigned long long want = a.shard_epoch * static_cast<unsigned long long>(a.x_slices);
+        const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
+        while (ld_acquire_sys(a.arrive) < want) {
+            if (dev::globaltimer_ns() > deadline) {
+                atomicOr(a.shard_status, 1u);
+                break;
+            }
+            __nanosleep(100);
+        }
+    }
+    __syncwarp();
 }
 
-// Sharded epilogue (last CTA): copy this rank's finished y rows into every peer's gathered y, then
-// publish the step's epoch in each peer's flag word for this rank (system-scope release).  The rows
-// start at any element offset; all gathered buffers share one layout, so source and destination
-// have the same alignment: a byte head, 16-byte body, byte tail.  Loads bypass L1 (__ldcg), since
-// the rows were written by other CTAs.
-__device__ __forceinline__ void shard_push_y(const GemvArgs &a) {
-    if (a.shard_world <= 1) return;
-    const uint8_t *src = a.peer_y[a.shard_rank] + a.y_shard_off;
-    const int64_t bytes = a.y_shard_bytes;
-    const int64_t head = min(static_cast<int64_t>((16 - (a.y_shard_off & 15)) & 15), bytes);
-    const int64_t n16 = (bytes - head) / 16;
-    const int64_t tail = head + n16 * 16;
-    for (int p = 0; p < a.shard_world; ++p) {
-        if (p == a.shard_rank) continue;
-        uint8_t *dst = a.peer_y[p] + a.y_shard_off;
-        if (threadIdx.x < head) dst[threadIdx.x] = __ldcg(src + threadIdx.x);
-        for (int64_t k = threadIdx.x; k < n16; k += blockDim.x)
-            reinterpret_cast<uint4 *>(dst + head)[k] = __ldcg(reinterpret_cast<const uint4 *>(src + head) + k);
-        for (int64_t k = tail + threadIdx.x; k < bytes; k += blockDim.x) dst[k] = __ldcg(src + k);
+// Sharded epilogue (last CTA): wait (bounded) until every peer's chunks of this step have arrived.
+template <bool SH> __device__ __forceinline__ void shard_final_wait(const GemvArgs &a) {
+    if (!SH) return;
+    const int p = threadIdx.x;
+    if (p < a.shard_world && p != a.shard_rank) {
+        const unsigned long long want = a.shard_epoch * a.chunks_of[p];
+        const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
+        while (ld_acquire_sys(a.arrive + 1 + p) < want) {
+            if (dev::globaltimer_ns() > deadline) {
+                atomicOr(a.shard_status, 2u);
+                break;
+            }
+            __nanosleep(100);
+        }
     }
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x < a.shard_world) st_release_sys(a.peer_flags[threadIdx.x] + 1 + a.shard_rank, a.shard_epoch);
 }
 
 __device__ __forceinline__ unsigned long long ld_claim(const unsigned long long *p) {
@@ -491,7 +600,7 @@ __device__ __forceinline__ int warp_claim_any(const GemvArgs &a, unsigned long l
     return -1;
 }
 
-template <int DT_IN, int DT_OUT, bool SPLIT>
+template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int s_slot;
@@ -517,11 +626,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
             s_slot = got;
             s_epoch = E;
             s_count = 0;
-            shard_wait_x(a);
         }
+        shard_prologue<SH>(a, lane);
     }
     __syncthreads();
-    if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT>(a, s_slot, warp, nwarps, lane, smem);
+    if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -540,10 +649,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     const int n_left = s_count;
     if (tid == 0 && n_left) atomicAdd(a.ctl + 2, static_cast<unsigned long long>(n_left));
     for (int k = 0; k < n_left; ++k) {
-        run_slot<DT_IN, DT_OUT, SPLIT>(a, s_list[k], warp, nwarps, lane, smem);
+        run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
         __syncthreads();
     }
-    shard_push_y(a);
+    shard_final_wait<SH>(a);
     if (tid == 0) {
         a.ctl[1] = 0ull;
         __threadfence();
@@ -553,23 +662,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
 
 using KernelFn = void (*)(GemvArgs);
 
-template <int DI, int DO> KernelFn pick_split(bool split) {
-    return split ? k_gemv<DI, DO, true> : k_gemv<DI, DO, false>;
+// SH: the peer-memory sharded variant (its bookkeeping is compiled out of the others).
+template <int DI, int DO> KernelFn pick_split(bool split, bool sh) {
+    if (sh) return split ? k_gemv<DI, DO, true, true> : k_gemv<DI, DO, false, true>;
+    return split ? k_gemv<DI, DO, true, false> : k_gemv<DI, DO, false, false>;
 }
 
-template <int DI> KernelFn pick_out(int dout, bool split) {
+template <int DI> KernelFn pick_out(int dout, bool split, bool sh) {
     switch (dout) {
-    case L2D_F32: return pick_split<DI, L2D_F32>(split);
-    case L2D_F16: return pick_split<DI, L2D_F16>(split);
-    default: return pick_split<DI, L2D_BF16>(split);
+    case L2D_F32: return pick_split<DI, L2D_F32>(split, sh);
+    case L2D_F16: return pick_split<DI, L2D_F16>(split, sh);
+    default: return pick_split<DI, L2D_BF16>(split, sh);
     }
 }
 
-KernelFn pick_kernel(int din, int dout, bool split) {
+KernelFn pick_kernel(int din, int dout, bool split, bool sh = false) {
     switch (din) {
-    case L2D_F32: return pick_out<L2D_F32>(dout, split);
-    case L2D_F16: return pick_out<L2D_F16>(dout, split);
-    default: return pick_out<L2D_BF16>(dout, split);
+    case L2D_F32: return pick_out<L2D_F32>(dout, split, sh);
+    case L2D_F16: return pick_out<L2D_F16>(dout, split, sh);
+    default: return pick_out<L2D_BF16>(dout, split, sh);
     }
 }
 
@@ -886,8 +997,8 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
         if (max_nb * rb16 <= kXSmemMax) p->x_smem_bytes = static_cast<size_t>(max_nb * rb16);
     }
-    for (bool split : {false, true}) {
-        const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, split), d.device);
+    for (int v = 0; v < 4; ++v) {
+        const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, v & 1, v >> 1), d.device);
         if (fe != L2D_OK) {
             cudaFree(p->dev_block);
             delete p;
@@ -974,7 +1085,8 @@ int check_args(const GemvArgs &a) {
     if (!a.x || !a.y || !a.sm_slot || !a.pair || !a.claim || !a.ctl || a.n_slots <= 0 ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
-    if (a.shard_world > 1 && (!a.x_flag || !a.peer_y || !a.peer_flags || !a.shard_status))
+    if (a.shard_world > 1 && (!a.arrive || !a.peer_arrive || !a.peer_x || !a.peer_y || !a.chunks_of ||
+                              !a.chunk_cnt || !a.shard_status || a.x_slices <= 0))
         return set_error(L2D_ERR_INVALID, "sharded gemv arguments incomplete (internal error)");
     return L2D_OK;
 }
@@ -982,7 +1094,7 @@ int check_args(const GemvArgs &a) {
 int launch_args(l2d_plan *p, const GemvArgs &a, bool split, void *stream) {
     const int chk = check_args(a);
     if (chk != L2D_OK) return chk;
-    KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split);
+    KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split, a.shard_world > 1);
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != p->device) cudaSetDevice(p->device);
@@ -1000,19 +1112,24 @@ int plan_out_bytes(const l2d_plan *p) { return p->eb_out; }
 size_t gemv_args_size() { return sizeof(GemvArgs); }
 
 // Adds the peer-memory sharding fields to arguments made by build_args.
-int shard_fill_args(GemvArgs *a, int world, int rank, unsigned long long epoch, const unsigned long long *x_flag,
-                    uint8_t *const *peer_y, unsigned long long *const *peer_flags, int64_t y_off, int64_t y_bytes,
-                    uint32_t *status, uint64_t timeout_ns) {
-    a->shard_world = world;
-    a->shard_rank = rank;
-    a->shard_epoch = epoch;
-    a->x_flag = x_flag;
-    a->peer_y = peer_y;
-    a->peer_flags = peer_flags;
-    a->y_shard_off = y_off;
-    a->y_shard_bytes = y_bytes;
-    a->shard_status = status;
-    a->shard_timeout_ns = timeout_ns;
+int shard_fill_args(GemvArgs *a, const ShardArgs &sh) {
+    a->shard_world = sh.world;
+    a->shard_rank = sh.rank;
+    a->shard_epoch = sh.epoch;
+    a->arrive = sh.arrive;
+    a->peer_arrive = sh.peer_arrive;
+    a->peer_x = sh.peer_x;
+    a->peer_y = sh.peer_y;
+    a->chunks_of = sh.chunks_of;
+    a->chunk_cnt = sh.chunk_cnt;
+    a->y_shard_off = sh.y_shard_off;
+    a->x_bytes = sh.x_bytes;
+    a->chunk_shift = sh.chunk_shift;
+    a->x_slices = sh.x_slices;
+    a->shard_status = sh.status;
+    a->shard_timeout_ns = sh.timeout_ns;
+    if (sh.world > 1 && a->n_slots < sh.x_slices)
+        return set_error(L2D_ERR_UNSUPPORTED, "sharded gemv needs >= %d CTAs, plan has %d", sh.x_slices, a->n_slots);
     return L2D_OK;
 }
 

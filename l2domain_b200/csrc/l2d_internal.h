@@ -30,6 +30,22 @@ inline int parity_domain(uint32_t mask, uint64_t addr, int attr) {
 
 inline int lowest_bit_or(uint32_t mask, int fallback) { return mask ? __builtin_ctz(mask) : fallback; }
 
+// Peer-memory sharding fields of one l2d_gemv_sharded step (device pointers unless noted).
+struct ShardArgs {
+    int world, rank;
+    unsigned long long epoch;
+    unsigned long long *arrive;
+    unsigned long long *const *peer_arrive;
+    uint8_t *const *peer_x;
+    uint8_t *const *peer_y;
+    const unsigned long long *chunks_of;
+    unsigned long long *chunk_cnt;
+    int64_t y_shard_off, x_bytes;
+    int chunk_shift, x_slices;
+    uint32_t *status;
+    uint64_t timeout_ns;
+};
+
 }  // namespace l2d
 
 #define L2D_CUDA_TRY(call)                                                                                   \

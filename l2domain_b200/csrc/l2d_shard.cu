@@ -2,17 +2,20 @@
 //
 // The reference has no multi-GPU path.  The row-sharded configuration broadcasts x from rank 0 and
 // gathers the y shards on every rank; instead of a broadcast and an all-gather launched around the
-// GEMV, every rank maps the other ranks' shard buffers (cudaIpcOpenMemHandle) and the exchange is
-// folded into the step:
-//   1. rank 0 pushes x into every peer's x buffer (plain 16-byte stores over NVLink) and raises the
-//      step's epoch in each peer's x flag (system-scope release);
-//   2. every rank runs the GEMV of its rows; its CTAs first wait (bounded) for the x flag, and its
-//      last CTA copies the finished y rows into every peer's gathered y and raises its done flag
-//      there;
-//   3. a one-warp kernel waits (bounded) until every peer's done flag carries the epoch.
-// x and y are double-buffered by the parity of the step's epoch, so a step never overwrites data a
-// peer may still be reading from the step before.  Every wait is bounded by %globaltimer; a
-// timeout sets a status bit (l2d_shard_status) and the kernels return.  No TMA or bulk-copy load
+// GEMV, every rank maps the other ranks' shard buffers (cudaIpcOpenMemHandle) and one GEMV launch
+// per rank and step does the exchange while it computes:
+//   * rank 0's first kXSlices CTAs each push one slice of x into every peer's x buffer and count it
+//     in that peer's x arrival counter (system-scope release); the other ranks' CTAs wait for all
+//     slices before they stage x;
+//   * every final y store counts its row in a chunk counter; the warp that completes a chunk of
+//     2^kChunkShift rows pushes those rows into every peer's gathered y and counts the chunk there,
+//     so the gather runs under the GEMV;
+//   * the last CTA waits until every peer's chunks of the step have arrived.
+// x and y are double-buffered by the parity of the step number, so a step never overwrites data a
+// peer may still read from the step before (a rank enters step e+1 only after every peer's step-e
+// rows arrived, i.e. after every peer finished reading step e-1's buffers).  Arrival counters only
+// grow: the target of step e is e times the per-step count.  Every wait is bounded by %globaltimer;
+// a timeout sets a status bit (l2d_shard_status) and the kernel returns.  No TMA or bulk-copy load
 // touches peer memory: only plain loads and stores.
 #include "l2d_device.cuh"
 #include "l2d_internal.h"
@@ -33,20 +36,22 @@ int launch_args(l2d_plan *p, const GemvArgs &a, bool split, void *stream);
 int plan_device(const l2d_plan *p);
 int64_t plan_rows(const l2d_plan *p);
 const l2d_gemv_desc &plan_desc(const l2d_plan *p);
-int shard_fill_args(GemvArgs *a, int world, int rank, unsigned long long epoch, const unsigned long long *x_flag,
-                    uint8_t *const *peer_y, unsigned long long *const *peer_flags, int64_t y_off, int64_t y_bytes,
-                    uint32_t *status, uint64_t timeout_ns);
+int shard_fill_args(GemvArgs *a, const ShardArgs &sh);
 size_t gemv_args_size();
 
 namespace shard {
 
 constexpr uint32_t kMagic = 0x4c32445du;  // "L2D]"
+constexpr uint32_t kVersion = 2;
 constexpr int kMaxWorld = 64;
+constexpr int kChunkShift = 9;  // 512 rows per pushed chunk
+constexpr int kXSlices = 32;    // x is pushed in this many slices, one per CTA of rank 0
 
 struct Blob {
     uint32_t magic, version;
     int32_t pid, rank, world, device;
-    int64_t bytes;
+    int64_t bytes, rows;
+    int32_t chunk_shift, x_slices;
     uint64_t raw;  // device address in the exporting process (used when importer == exporter)
     cudaIpcMemHandle_t handle;
 };
@@ -57,45 +62,41 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Rank 0: x into every peer's x buffer of this parity, then the epoch into each peer's x flag.
-__global__ void k_push_x(const uint8_t *x, int64_t bytes, uint8_t *const *peer_x, unsigned long long *const *peer_flags,
-                         int world, unsigned long long epoch) {
-    const int64_t n16 = bytes / 16;
-    for (int p = 1; p < world; ++p) {
-        uint8_t *dst = peer_x[p];
-        for (int64_t k = threadIdx.x; k < n16; k += blockDim.x)
-            reinterpret_cast<uint4 *>(dst)[k] = reinterpret_cast<const uint4 *>(x)[k];
-        for (int64_t k = n16 * 16 + threadIdx.x; k < bytes; k += blockDim.x) dst[k] = x[k];
+// The step of a rank without rows (M_total < world): rank 0 still pushes x (kXSlices CTAs of one
+// warp, as the GEMV prologue does), and CTA 0 waits for the peers' chunks.
+__global__ void k_shard_idle(ShardArgs sh, const uint8_t *x) {
+    const int lane = threadIdx.x;
+    if (sh.rank == 0 && sh.world > 1) {
+        const int64_t n16 = sh.x_bytes / 16;
+        const int64_t lo = n16 * blockIdx.x / sh.x_slices, hi = n16 * (blockIdx.x + 1) / sh.x_slices;
+        const bool tail = static_cast<int>(blockIdx.x) == sh.x_slices - 1;
+        for (int p = 1; p < sh.world; ++p) {
+            for (int64_t k = lo + lane; k < hi; k += 32)
+                reinterpret_cast<uint4 *>(sh.peer_x[p])[k] = reinterpret_cast<const uint4 *>(x)[k];
+            if (tail)
+                for (int64_t k = n16 * 16 + lane; k < sh.x_bytes; k += 32) sh.peer_x[p][k] = x[k];
+        }
+        __threadfence_system();
+        __syncwarp();
+        if (lane >= 1 && lane < sh.world) red_release_sys_add(sh.peer_arrive[lane], 1ull);
     }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x >= 1 && threadIdx.x < world) st_release_sys(peer_flags[threadIdx.x], epoch);
-}
-
-// Every rank: wait until each peer has pushed its y rows of this step (bounded).
-__global__ void k_wait_done(const unsigned long long *flags, int world, int rank, unsigned long long epoch,
-                            uint32_t *status, uint64_t timeout_ns) {
-    if (threadIdx.x != 0) return;
-    const uint64_t deadline = dev::globaltimer_ns() + timeout_ns;
-    for (int p = 0; p < world; ++p) {
-        if (p == rank) continue;
-        while (ld_acquire_sys(flags + 1 + p) < epoch) {
+    if (blockIdx.x != 0) return;
+    for (int p = lane; p < sh.world; p += 32) {
+        if (p == sh.rank) continue;
+        const unsigned long long want = sh.epoch * sh.chunks_of[p];
+        const uint64_t deadline = dev::globaltimer_ns() + sh.timeout_ns;
+        while (ld_acquire_sys(sh.arrive + 1 + p) < want) {
             if (dev::globaltimer_ns() > deadline) {
-                atomicOr(status, 2u);
-                return;
+                atomicOr(sh.status, 2u);
+                break;
             }
-            __nanosleep(200);
+            __nanosleep(100);
         }
     }
-}
-
-// A rank without rows still publishes its (empty) part so the peers' waits end.
-__global__ void k_raise_done(unsigned long long *const *peer_flags, int world, int rank, unsigned long long epoch) {
-    if (threadIdx.x < world && threadIdx.x != rank) st_release_sys(peer_flags[threadIdx.x] + 1 + rank, epoch);
 }
 
 size_t up256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -108,12 +109,16 @@ struct l2d_shard {
     int64_t M_total = 0, row0 = 0, rows = 0, N = 0;
     int dtype_in = 0, dtype_out = 0, eb_in = 4, eb_out = 4;
     uint64_t timeout_ns = 0;
-    uint8_t *base = nullptr;  // local shared allocation
+    uint8_t *base = nullptr;  // shared allocation: arrival counters, x[2], y[2]
     size_t bytes = 0;
-    size_t off_flags = 0, off_x[2] = {0, 0}, off_y[2] = {0, 0};
-    std::vector<uint8_t *> peer;     // [world] peer bases in this process's address space
-    std::vector<bool> opened;        // opened through IPC (closed on destroy)
-    uint8_t *tables = nullptr;       // device: peer_x[2][world], peer_y[2][world], peer_flags[world], status
+    size_t off_arrive = 0, off_x[2] = {0, 0}, off_y[2] = {0, 0};
+    std::vector<uint8_t *> peer;  // [world] peer bases in this process's address space
+    std::vector<bool> opened;     // opened through IPC (closed on destroy)
+    // Local device tables: peer_x[2][world], peer_y[2][world], peer_arrive[world] (pointers),
+    // chunks_of[world] (u64), status (u32, padded to 16 bytes), chunk_cnt[own chunks] (u64).
+    uint8_t *tables = nullptr;
+    size_t off_chunks_of = 0, off_status = 0, off_cnt = 0, tables_bytes = 0;
+    int64_t own_chunks = 0;
     bool connected = false;
     unsigned long long epoch = 0;
 };
@@ -124,10 +129,16 @@ namespace {
 
 uint8_t **tab_x(l2d_shard *s, int par) { return reinterpret_cast<uint8_t **>(s->tables) + par * s->world; }
 uint8_t **tab_y(l2d_shard *s, int par) { return reinterpret_cast<uint8_t **>(s->tables) + (2 + par) * s->world; }
-unsigned long long **tab_flags(l2d_shard *s) {
+unsigned long long **tab_arrive(l2d_shard *s) {
     return reinterpret_cast<unsigned long long **>(s->tables) + 4 * s->world;
 }
-uint32_t *status_word(l2d_shard *s) { return reinterpret_cast<uint32_t *>(s->tables + 5 * s->world * sizeof(void *)); }
+unsigned long long *tab_chunks_of(l2d_shard *s) {
+    return reinterpret_cast<unsigned long long *>(s->tables + s->off_chunks_of);
+}
+uint32_t *status_word(l2d_shard *s) { return reinterpret_cast<uint32_t *>(s->tables + s->off_status); }
+unsigned long long *chunk_counters(l2d_shard *s) { return reinterpret_cast<unsigned long long *>(s->tables + s->off_cnt); }
+
+int64_t chunks_for(int64_t rows) { return (rows + (int64_t(1) << shard::kChunkShift) - 1) >> shard::kChunkShift; }
 
 struct DeviceScope {
     int prev = -1;
@@ -139,6 +150,27 @@ struct DeviceScope {
         if (prev >= 0) cudaSetDevice(prev);
     }
 };
+
+ShardArgs shard_args(l2d_shard *s, int par, unsigned long long e) {
+    ShardArgs sh;
+    std::memset(&sh, 0, sizeof sh);
+    sh.world = s->world;
+    sh.rank = s->rank;
+    sh.epoch = e;
+    sh.arrive = reinterpret_cast<unsigned long long *>(s->base + s->off_arrive);
+    sh.peer_arrive = tab_arrive(s);
+    sh.peer_x = tab_x(s, par);
+    sh.peer_y = tab_y(s, par);
+    sh.chunks_of = tab_chunks_of(s);
+    sh.chunk_cnt = chunk_counters(s);
+    sh.y_shard_off = s->row0 * s->eb_out;
+    sh.x_bytes = s->N * s->eb_in;
+    sh.chunk_shift = shard::kChunkShift;
+    sh.x_slices = shard::kXSlices;
+    sh.status = status_word(s);
+    sh.timeout_ns = s->timeout_ns;
+    return sh;
+}
 
 }  // namespace
 
@@ -173,7 +205,7 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
     s->eb_out = elem_bytes(dtype_out);
     s->timeout_ns = static_cast<uint64_t>(timeout_ms ? timeout_ms : 2000u) * 1000000ull;
     size_t off = 0;
-    s->off_flags = off;
+    s->off_arrive = off;
     off += shard::up256((1 + world) * sizeof(unsigned long long));
     for (int par = 0; par < 2; ++par) {
         s->off_x[par] = off;
@@ -184,11 +216,17 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(M_total, 1)) * s->eb_out);
     }
     s->bytes = off;
+    s->own_chunks = chunks_for(rows);
+    s->off_chunks_of = 5 * world * sizeof(void *);
+    s->off_status = s->off_chunks_of + world * sizeof(unsigned long long);
+    s->off_cnt = s->off_status + 16;
+    s->tables_bytes = s->off_cnt + std::max<int64_t>(s->own_chunks, 1) * sizeof(unsigned long long);
     cudaError_t e = cudaMalloc(&s->base, s->bytes);
     if (e == cudaSuccess) e = cudaMemset(s->base, 0, s->bytes);
-    if (e == cudaSuccess) e = cudaMalloc(&s->tables, 5 * world * sizeof(void *) + 256);
-    if (e == cudaSuccess) e = cudaMemset(s->tables, 0, 5 * world * sizeof(void *) + 256);
+    if (e == cudaSuccess) e = cudaMalloc(&s->tables, s->tables_bytes);
+    if (e == cudaSuccess) e = cudaMemset(s->tables, 0, s->tables_bytes);
     if (e != cudaSuccess) {
+        if (s->tables) cudaFree(s->tables);
         if (s->base) cudaFree(s->base);
         delete s;
         return set_error(L2D_ERR_CUDA, "shard buffers: %s", cudaGetErrorString(e));
@@ -205,18 +243,21 @@ int l2d_shard_handle(const l2d_shard *s, void *blob, size_t cap, size_t *len) {
     if (!s || !len) return set_error(L2D_ERR_INVALID, "shard_handle: null argument");
     *len = sizeof(shard::Blob);
     if (!blob) return L2D_OK;
-    if (cap < sizeof(shard::Blob)) return set_error(L2D_ERR_INVALID, "handle buffer of %zu bytes < %zu", cap,
-                                                    sizeof(shard::Blob));
+    if (cap < sizeof(shard::Blob))
+        return set_error(L2D_ERR_INVALID, "handle buffer of %zu bytes < %zu", cap, sizeof(shard::Blob));
     DeviceScope scope(s->device);
     shard::Blob b;
     std::memset(&b, 0, sizeof b);
     b.magic = shard::kMagic;
-    b.version = 1;
+    b.version = shard::kVersion;
     b.pid = static_cast<int32_t>(getpid());
     b.rank = s->rank;
     b.world = s->world;
     b.device = s->device;
     b.bytes = static_cast<int64_t>(s->bytes);
+    b.rows = s->rows;
+    b.chunk_shift = shard::kChunkShift;
+    b.x_slices = shard::kXSlices;
     b.raw = reinterpret_cast<uint64_t>(s->base);
     L2D_CUDA_TRY(cudaIpcGetMemHandle(&b.handle, s->base));
     std::memcpy(blob, &b, sizeof b);
@@ -230,32 +271,42 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
                          sizeof(shard::Blob));
     DeviceScope scope(s->device);
     const pid_t me = getpid();
+    std::vector<unsigned long long> chunks(s->world, 0);
+    int64_t rows_sum = 0;
     for (int r = 0; r < s->world; ++r) {
         shard::Blob b;
         std::memcpy(&b, static_cast<const uint8_t *>(blobs) + r * blob_len, sizeof b);
-        if (b.magic != shard::kMagic || b.version != 1 || b.rank != r || b.world != s->world ||
-            b.bytes != static_cast<int64_t>(s->bytes))
+        if (b.magic != shard::kMagic || b.version != shard::kVersion || b.rank != r || b.world != s->world ||
+            b.bytes != static_cast<int64_t>(s->bytes) || b.chunk_shift != shard::kChunkShift ||
+            b.x_slices != shard::kXSlices || b.rows < 0)
             return set_error(L2D_ERR_INVALID, "shard blob %d does not match this shard layout", r);
-        if (r == s->rank) continue;
-        if (s->peer[r]) continue;
+        chunks[r] = static_cast<unsigned long long>(chunks_for(b.rows));
+        rows_sum += b.rows;
+        if (r == s->rank || s->peer[r]) continue;
         if (b.pid == static_cast<int32_t>(me)) {
             s->peer[r] = reinterpret_cast<uint8_t *>(b.raw);  // same process: the address is valid here
         } else {
             void *p = nullptr;
             cudaError_t e = cudaIpcOpenMemHandle(&p, b.handle, cudaIpcMemLazyEnablePeerAccess);
-            if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "opening rank %d's buffers: %s", r, cudaGetErrorString(e));
+            if (e != cudaSuccess)
+                return set_error(L2D_ERR_CUDA, "opening rank %d's buffers: %s", r, cudaGetErrorString(e));
             s->peer[r] = static_cast<uint8_t *>(p);
             s->opened[r] = true;
         }
     }
+    if (rows_sum != s->M_total)
+        return set_error(L2D_ERR_INVALID, "the ranks' rows add up to %lld, not M_total = %lld",
+                         static_cast<long long>(rows_sum), static_cast<long long>(s->M_total));
     std::vector<uint8_t *> host(5 * s->world);
     for (int par = 0; par < 2; ++par)
         for (int r = 0; r < s->world; ++r) {
             host[par * s->world + r] = s->peer[r] + s->off_x[par];
             host[(2 + par) * s->world + r] = s->peer[r] + s->off_y[par];
         }
-    for (int r = 0; r < s->world; ++r) host[4 * s->world + r] = s->peer[r] + s->off_flags;
+    for (int r = 0; r < s->world; ++r) host[4 * s->world + r] = s->peer[r] + s->off_arrive;
     L2D_CUDA_TRY(cudaMemcpy(s->tables, host.data(), host.size() * sizeof(void *), cudaMemcpyHostToDevice));
+    L2D_CUDA_TRY(cudaMemcpy(tab_chunks_of(s), chunks.data(), chunks.size() * sizeof(unsigned long long),
+                            cudaMemcpyHostToDevice));
     s->connected = true;
     return L2D_OK;
 }
@@ -271,43 +322,36 @@ int l2d_shard_next_parity(const l2d_shard *s) { return s ? static_cast<int>((s->
 
 int l2d_gemv_sharded(l2d_plan *plan, l2d_shard *s, int mode, void *stream, int *parity) {
     clear_error();
-    if (!plan || !s) return set_error(L2D_ERR_INVALID, "gemv_sharded: null plan or shard");
-    if (!s->connected && s->world > 1) return set_error(L2D_ERR_INVALID, "gemv_sharded: shard not connected");
-    const l2d_gemv_desc &d = plan_desc(plan);
-    if (plan_device(plan) != s->device || plan_rows(plan) != s->rows || d.N != s->N || d.dtype_in != s->dtype_in ||
-        d.dtype_out != s->dtype_out || d.batch > 1)
-        return set_error(L2D_ERR_INVALID, "plan and shard disagree (device, rows, N, dtypes or batch)");
-    DeviceScope scope(s->device);
-    const unsigned long long e = ++s->epoch;
-    const int par = static_cast<int>(e & 1ull);
-    if (parity) *parity = par;
-    cudaStream_t cs = static_cast<cudaStream_t>(stream);
-    uint8_t *x = s->base + s->off_x[par];
-    uint8_t *yfull = s->base + s->off_y[par];
-    if (s->world > 1 && s->rank == 0) {
-        shard::k_push_x<<<1, 256, 0, cs>>>(x, s->N * s->eb_in, tab_x(s, par), tab_flags(s), s->world, e);
-        L2D_CUDA_TRY(cudaGetLastError());
+    if (!s) return set_error(L2D_ERR_INVALID, "gemv_sharded: null shard");
+    if (!s->connected) return set_error(L2D_ERR_INVALID, "gemv_sharded: shard not connected");
+    if (s->rows > 0) {
+        if (!plan) return set_error(L2D_ERR_INVALID, "gemv_sharded: null plan");
+        const l2d_gemv_desc &d = plan_desc(plan);
+        if (plan_device(plan) != s->device || plan_rows(plan) != s->rows || d.N != s->N ||
+            d.dtype_in != s->dtype_in || d.dtype_out != s->dtype_out || d.batch > 1)
+            return set_error(L2D_ERR_INVALID, "plan and shard disagree (device, rows, N, dtypes or batch)");
     }
+    DeviceScope scope(s->device);
+    const unsigned long long e = s->epoch + 1;
+    const int par = static_cast<int>(e & 1ull);
+    cudaStream_t cs = static_cast<cudaStream_t>(stream);
+    const ShardArgs sh = shard_args(s, par, e);
     if (s->rows > 0) {
         std::vector<uint8_t> buf(gemv_args_size());
         GemvArgs *a = reinterpret_cast<GemvArgs *>(buf.data());
         bool split = false;
-        int st = build_args(plan, d.A, x, yfull + s->row0 * s->eb_out, mode, a, &split);
-        if (st != L2D_OK) return st;
-        shard_fill_args(a, s->world, s->rank, e, reinterpret_cast<const unsigned long long *>(s->base + s->off_flags),
-                        tab_y(s, par), tab_flags(s), s->row0 * s->eb_out, s->rows * s->eb_out, status_word(s),
-                        s->timeout_ns);
-        st = launch_args(plan, *a, split, stream);
+        const l2d_gemv_desc &d = plan_desc(plan);
+        int st = build_args(plan, d.A, s->base + s->off_x[par], s->base + s->off_y[par] + sh.y_shard_off, mode, a,
+                            &split);
+        if (st == L2D_OK) st = shard_fill_args(a, sh);
+        if (st == L2D_OK) st = launch_args(plan, *a, split, stream);
         if (st != L2D_OK) return st;
     } else if (s->world > 1) {
-        shard::k_raise_done<<<1, 64, 0, cs>>>(tab_flags(s), s->world, s->rank, e);
+        shard::k_shard_idle<<<shard::kXSlices, 32, 0, cs>>>(sh, s->base + s->off_x[par]);
         L2D_CUDA_TRY(cudaGetLastError());
     }
-    if (s->world > 1) {
-        shard::k_wait_done<<<1, 32, 0, cs>>>(reinterpret_cast<const unsigned long long *>(s->base + s->off_flags),
-                                             s->world, s->rank, e, status_word(s), s->timeout_ns);
-        L2D_CUDA_TRY(cudaGetLastError());
-    }
+    s->epoch = e;  // only a launched step advances the step number (all ranks must stay in step)
+    if (parity) *parity = par;
     return L2D_OK;
 }
 

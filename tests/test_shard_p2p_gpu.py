@@ -6,7 +6,8 @@
   sets, never by a fault;
 * two GPUs (skipped with fewer): two processes exchange IPC handles over NCCL and run three
   steps; every rank's gathered y must equal the all-gather of the planned GEMV's shards exactly.
-  The row split is ragged (5003 rows), so a shard starts at a byte offset that is not 16-aligned.
+  The row split is ragged (5003 rows), so a shard starts at a byte offset that is not 16-aligned;
+  with one row in all, rank 1 owns none and still takes part in every step.
 """
 import os
 import socket
@@ -137,11 +138,13 @@ def _two_gpu_worker(rank, world, port, M, N, q):
         dist.destroy_process_group()
 
 
-def test_two_gpus_gather_equals_nccl_allgather():
+@pytest.mark.parametrize("M", [5003, 1])
+def test_two_gpus_gather_equals_nccl_allgather(M):
+    """M = 1 leaves rank 1 without rows: it still takes part in every step."""
     need_gpu(2)
     import torch.multiprocessing as mp
 
-    M, N, world = 5003, 8192, 2
+    N, world = 8192, 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
