@@ -288,11 +288,6 @@ struct Pending {
     bool active;
 };
 
-// Sharded bookkeeping of each warp, kept in shared memory (the unit loop has no registers to spare):
-// [0], [1] chunks the warp completed and still has to push (-1 = none); [2] resolve() stored row
-// `Pending::row` inside the unit loop, to be counted once the loop is done.
-__shared__ int s_shard_warp[kThreads / 32][3];
-
 __device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -300,7 +295,7 @@ __device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsig
 // Sharded: copies chunk c of this rank's y rows into every peer's gathered y, then counts it in
 // each peer's arrival counter for this rank.  Called by `nthr` threads with ids 0..nthr-1 (a warp,
 // or a single thread); all gathered buffers share one layout, so source and destination have the
-// same alignment.  The rows were stored by other warps, which fenced before counting them: the
+// same alignment.  The rows were stored by other CTAs, which fenced before counting them: the
 // caller saw the count complete, so a fence here and L2 loads (__ldcg) read the final values.
 template <int DT_OUT> __device__ void push_chunk(const GemvArgs &a, int c, int t, int nthr) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
@@ -332,32 +327,47 @@ template <int DT_OUT> __device__ void push_chunk(const GemvArgs &a, int c, int t
         if (p != a.shard_rank) red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, 1ull);
 }
 
-// Sharded, one thread (lane 0) after a final y store of `row`: counts the row in its chunk and, if
-// it completed the chunk, hands the chunk to the warp (pend.push).  A warp stores at most two final
-// rows between two flush points (the previous row's deferred one and its own), so two slots do.
-template <int DT_OUT, bool SH> __device__ __forceinline__ void count_row(const GemvArgs &a, int64_t row, Pending &pend) {
-    if (!SH) return;
-    const int c = static_cast<int>(row >> a.chunk_shift);
-    const int64_t r0 = static_cast<int64_t>(c) << a.chunk_shift;
-    const int64_t rows = min(static_cast<int64_t>(1) << a.chunk_shift, a.rows_total - r0);
-    __threadfence();  // the y store before its count
-    const unsigned long long old = atomicAdd(a.chunk_cnt + c, 1ull);
-    if (old + 1ull != a.shard_epoch * static_cast<unsigned long long>(rows)) return;
-    int *w = s_shard_warp[threadIdx.x >> 5];
-    w[w[0] < 0 ? 0 : 1] = c;
+// Spill rows in [lo, hi): the spill predicate telescopes, floor(hi num/den) - floor(lo num/den).
+__device__ __forceinline__ int64_t spills_in(const GemvArgs &a, int64_t lo, int64_t hi) {
+    return hi * a.spill_num / a.spill_den - lo * a.spill_num / a.spill_den;
 }
 
-// Warp-uniform point: push the chunks lane 0 completed, if any, with the whole warp.
-template <int DT_OUT, bool SH> __device__ __forceinline__ void flush_push(const GemvArgs &a, Pending &pend, int lane) {
-    if (!SH) return;
-    int *w = s_shard_warp[threadIdx.x >> 5];
-    __syncwarp();
-    const int c0 = w[0], c1 = w[1];
-    if (c0 < 0) return;
-    push_chunk<DT_OUT>(a, c0, lane, 32);
-    if (c1 >= 0) push_chunk<DT_OUT>(a, c1, lane, 32);
-    __syncwarp();
-    if (lane == 0) w[0] = w[1] = -1;
+// Sharded, the whole CTA at the end of a slot [r0, r1) whose rows are all visited and whose last
+// deferred row is resolved (every warp fenced its y stores, then a CTA barrier).  Row r of a split
+// call is final once both groups visited it (spill rows: once the bigger group did), so chunk c is
+// final when the visits counted into chunk_cnt[c] reach 2 rows(c) - spills(c) per step (rows(c)
+// unsplit).  Each slot adds its visits per chunk in closed form; the CTA that completes a chunk
+// pushes it to the peers.
+// The slot's row range and group role are read back from shared memory (s_slot_info, written when
+// the slot started) so they need no registers during the row loop.
+__shared__ long long s_slot_info[3];  // r0, r1, small group
+
+template <int DT_OUT, bool SPLIT>
+__device__ __forceinline__ void shard_count_slot(const GemvArgs &a, int warp, int nwarps, int lane) {
+    __shared__ int s_n;
+    __shared__ int s_done[64];
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    const int64_t r0 = s_slot_info[0], r1 = s_slot_info[1];
+    const bool small_grp = s_slot_info[2] != 0;
+    const int64_t cs = static_cast<int64_t>(1) << a.chunk_shift;
+    const int64_t c_first = r0 >> a.chunk_shift, c_last = (r1 - 1) >> a.chunk_shift;
+    for (int64_t c = c_first + threadIdx.x; c <= c_last; c += blockDim.x) {
+        const int64_t cr0 = c * cs, cr1 = min(cr0 + cs, a.rows_total);
+        const int64_t lo = max(r0, cr0), hi = min(r1, cr1);
+        const int64_t visits = (hi - lo) - (small_grp ? spills_in(a, lo, hi) : 0);
+        const int64_t expect = SPLIT ? 2 * (cr1 - cr0) - spills_in(a, cr0, cr1) : (cr1 - cr0);
+        if (visits <= 0) continue;
+        const unsigned long long old = atomicAdd(a.chunk_cnt + c, static_cast<unsigned long long>(visits));
+        if (old + static_cast<unsigned long long>(visits) == a.shard_epoch * static_cast<unsigned long long>(expect)) {
+            const int k = atomicAdd(&s_n, 1);
+            if (k < 64) s_done[k] = static_cast<int>(c);
+        }
+    }
+    __syncthreads();
+    const int n = min(s_n, 64);
+    for (int k = warp; k < n; k += nwarps) push_chunk<DT_OUT>(a, s_done[k], lane, 32);
+    __syncthreads();
 }
 
 // Returns true when it stored the final y of row p.row.
@@ -375,7 +385,7 @@ template <int DT_OUT> __device__ __forceinline__ bool resolve(const GemvArgs &a,
 
 // One row of A for one domain group.  SPLIT: the row is shared by both groups (false for the
 // unsplit kernel and for spill rows, which the bigger group takes whole).
-template <int DT_IN, int DT_OUT, bool SH>
+template <int DT_IN, int DT_OUT>
 __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool SPLIT, int grp, int lane,
                                          const uint8_t *xs, int64_t xs_b0, Pending &pend) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
@@ -390,10 +400,7 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     const uint64_t u0 = rs >> kUnitShift;
     const uint64_t u1 = (re + (1u << kUnitShift) - 1) >> kUnitShift;
     if (u0 == u1) {  // N == 0: y = 0, written once
-        if (lane == 0 && grp == 0) {
-            store_out<DT_OUT>(yp, 0.0f);
-            count_row<DT_OUT, SH>(a, row, pend);
-        }
+        if (lane == 0 && grp == 0) store_out<DT_OUT>(yp, 0.0f);
         return;
     }
     const uint8_t *abase = a.region_base + lane * 32;
@@ -428,7 +435,7 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
             for (int u = 0; u < kUnroll; ++u)
                 if (idx[u] >= 0) av[u] = ld_stream32(abase + ((ub + idx[u]) << kUnitShift));
             if (!resolved) {
-                if (lane == 0 && resolve<DT_OUT>(a, pend) && SH) s_shard_warp[threadIdx.x >> 5][2] = 1;
+                if (lane == 0) resolve<DT_OUT>(a, pend);
                 resolved = true;
             }
 #pragma unroll
@@ -453,21 +460,15 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     float sum = acc.total();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane != 0) return;
-    if (SH && s_shard_warp[threadIdx.x >> 5][2]) {  // the previous row, finished in the loop
-        s_shard_warp[threadIdx.x >> 5][2] = 0;
-        count_row<DT_OUT, SH>(a, pend.row, pend);
-    }
-    if (!saw_mine) return;
+    if (lane != 0 || !saw_mine) return;
     if (!SPLIT || !saw_other) {
         store_out<DT_OUT>(yp, sum);
-        count_row<DT_OUT, SH>(a, row, pend);
         return;
     }
     // Both domain groups own part of this row.  Each adds ~bits(partial) into its own 32-bit half
     // of the row's pair word; ~bits is never 0 for a value arithmetic produces, so the group that
     // finds the other half non-zero holds both partials and finishes the row (in resolve()).
-    if (!resolved && resolve<DT_OUT>(a, pend)) count_row<DT_OUT, SH>(a, pend.row, pend);
+    if (!resolved) resolve<DT_OUT>(a, pend);
     pend.old = atomicAdd(a.pair + row, static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp));
     pend.yp = yp;
     pend.row = row;
@@ -495,13 +496,13 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     }
     Pending pend;
     pend.active = false;
-    if (SH && lane == 0) {
-        int *w = s_shard_warp[warp];
-        w[0] = w[1] = -1;
-        w[2] = 0;
-    }
     // The smaller domain group skips the spill rows, which the bigger group takes whole.
     const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
+    if (SH && threadIdx.x == 0) {
+        s_slot_info[0] = r0;
+        s_slot_info[1] = r1;
+        s_slot_info[2] = small_grp;
+    }
     const int32_t step_phase =
         a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
     RowIter it;
@@ -509,14 +510,13 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     for (int64_t row = r0 + warp; row < r1; row += nwarps, it.advance(a, nwarps, step_phase)) {
         const bool spill = SPLIT && it.spill(a);
         if (spill && small_grp) continue;
-        gemv_row<DT_IN, DT_OUT, SH>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
-        flush_push<DT_OUT, SH>(a, pend, lane);
+        gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
     }
     if (lane == 0) {
-        if (resolve<DT_OUT>(a, pend)) count_row<DT_OUT, SH>(a, pend.row, pend);
+        resolve<DT_OUT>(a, pend);
         __threadfence();  // this warp's y stores are visible before the CTA reports done
     }
-    flush_push<DT_OUT, SH>(a, pend, lane);
+    if (SH) shard_count_slot<DT_OUT, SPLIT>(a, warp, nwarps, lane);
     if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
 }
 

@@ -7,9 +7,10 @@
 //   * rank 0's first kXSlices CTAs each push one slice of x into every peer's x buffer and count it
 //     in that peer's x arrival counter (system-scope release); the other ranks' CTAs wait for all
 //     slices before they stage x;
-//   * every final y store counts its row in a chunk counter; the warp that completes a chunk of
-//     2^kChunkShift rows pushes those rows into every peer's gathered y and counts the chunk there,
-//     so the gather runs under the GEMV;
+//   * when a CTA finishes a slot (a block of rows for one L2-domain group), it adds its row visits
+//     to the counters of the chunks the slot overlaps; the CTA that completes a chunk (at most
+//     kMaxChunks per rank) pushes its rows into every peer's gathered y and counts the chunk there,
+//     so the gather runs under the GEMV as slots finish;
 //   * the last CTA waits until every peer's chunks of the step have arrived.
 // x and y are double-buffered by the parity of the step number, so a step never overwrites data a
 // peer may still read from the step before (a rank enters step e+1 only after every peer's step-e
@@ -44,7 +45,8 @@ namespace shard {
 constexpr uint32_t kMagic = 0x4c32445du;  // "L2D]"
 constexpr uint32_t kVersion = 2;
 constexpr int kMaxWorld = 64;
-constexpr int kChunkShift = 9;  // 512 rows per pushed chunk
+constexpr int kMinChunkShift = 9;  // at least 512 rows per pushed chunk
+constexpr int kMaxChunks = 64;     // at most this many chunks per rank (the kernel's per-slot list)
 constexpr int kXSlices = 32;    // x is pushed in this many slices, one per CTA of rank 0
 
 struct Blob {
@@ -119,6 +121,7 @@ struct l2d_shard {
     uint8_t *tables = nullptr;
     size_t off_chunks_of = 0, off_status = 0, off_cnt = 0, tables_bytes = 0;
     int64_t own_chunks = 0;
+    int chunk_shift = 9;
     bool connected = false;
     unsigned long long epoch = 0;
 };
@@ -138,7 +141,12 @@ unsigned long long *tab_chunks_of(l2d_shard *s) {
 uint32_t *status_word(l2d_shard *s) { return reinterpret_cast<uint32_t *>(s->tables + s->off_status); }
 unsigned long long *chunk_counters(l2d_shard *s) { return reinterpret_cast<unsigned long long *>(s->tables + s->off_cnt); }
 
-int64_t chunks_for(int64_t rows) { return (rows + (int64_t(1) << shard::kChunkShift) - 1) >> shard::kChunkShift; }
+int chunk_shift_for(int64_t rows) {
+    int sh = shard::kMinChunkShift;
+    while (((rows + (int64_t(1) << sh) - 1) >> sh) > shard::kMaxChunks) ++sh;
+    return sh;
+}
+int64_t chunks_for(int64_t rows, int sh) { return (rows + (int64_t(1) << sh) - 1) >> sh; }
 
 struct DeviceScope {
     int prev = -1;
@@ -165,7 +173,7 @@ ShardArgs shard_args(l2d_shard *s, int par, unsigned long long e) {
     sh.chunk_cnt = chunk_counters(s);
     sh.y_shard_off = s->row0 * s->eb_out;
     sh.x_bytes = s->N * s->eb_in;
-    sh.chunk_shift = shard::kChunkShift;
+    sh.chunk_shift = s->chunk_shift;
     sh.x_slices = shard::kXSlices;
     sh.status = status_word(s);
     sh.timeout_ns = s->timeout_ns;
@@ -216,7 +224,8 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(M_total, 1)) * s->eb_out);
     }
     s->bytes = off;
-    s->own_chunks = chunks_for(rows);
+    s->chunk_shift = chunk_shift_for(rows);
+    s->own_chunks = chunks_for(rows, s->chunk_shift);
     s->off_chunks_of = 5 * world * sizeof(void *);
     s->off_status = s->off_chunks_of + world * sizeof(unsigned long long);
     s->off_cnt = s->off_status + 16;
@@ -256,7 +265,7 @@ int l2d_shard_handle(const l2d_shard *s, void *blob, size_t cap, size_t *len) {
     b.device = s->device;
     b.bytes = static_cast<int64_t>(s->bytes);
     b.rows = s->rows;
-    b.chunk_shift = shard::kChunkShift;
+    b.chunk_shift = s->chunk_shift;
     b.x_slices = shard::kXSlices;
     b.raw = reinterpret_cast<uint64_t>(s->base);
     L2D_CUDA_TRY(cudaIpcGetMemHandle(&b.handle, s->base));
@@ -277,10 +286,10 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
         shard::Blob b;
         std::memcpy(&b, static_cast<const uint8_t *>(blobs) + r * blob_len, sizeof b);
         if (b.magic != shard::kMagic || b.version != shard::kVersion || b.rank != r || b.world != s->world ||
-            b.bytes != static_cast<int64_t>(s->bytes) || b.chunk_shift != shard::kChunkShift ||
-            b.x_slices != shard::kXSlices || b.rows < 0)
+            b.bytes != static_cast<int64_t>(s->bytes) || b.chunk_shift < shard::kMinChunkShift ||
+            b.chunk_shift > 40 || b.x_slices != shard::kXSlices || b.rows < 0)
             return set_error(L2D_ERR_INVALID, "shard blob %d does not match this shard layout", r);
-        chunks[r] = static_cast<unsigned long long>(chunks_for(b.rows));
+        chunks[r] = static_cast<unsigned long long>(chunks_for(b.rows, b.chunk_shift));
         rows_sum += b.rows;
         if (r == s->rank || s->peer[r]) continue;
         if (b.pid == static_cast<int32_t>(me)) {
