@@ -226,7 +226,7 @@ L2D_API int l2d_gemv_noalloc(const l2d_gemv_desc *desc, const l2d_domain_map *ma
  *   -> l2d_shard_connect(all blobs in rank order) -> per step:
  *      rank 0 writes x into l2d_shard_buffers(l2d_shard_next_parity()) .x, then every rank calls
  *      l2d_gemv_sharded; after it (stream-ordered) the gathered y of all M_total rows is in that
- *      parity's .y buffer on every rank.  Consume it before the step after next on the same stream.
+ *      parity's .y buffer on every rank.  Consume it on the same stream before the next step.
  * Rank 0 pushes x to the peers over NVLink; each rank's GEMV waits for it, then pushes its y rows to
  * every peer; a last kernel waits for all peers' rows.  Every wait is bounded by timeout_ms (0 =
  * 2000 ms); a timeout sets a bit in l2d_shard_status (1: x never arrived, 2: a peer's rows never

@@ -395,7 +395,6 @@ int probe_addr_domains_impl(int device, const uint8_t *base, size_t valid_bytes,
         std::sort(fit_pages.begin(), fit_pages.end());
         fit_pages.erase(std::unique(fit_pages.begin(), fit_pages.end()), fit_pages.end());
     }
-    const uint8_t *fit_base = base;
     if (fit_pages.empty()) {
         // Temporary buffer: must sit above base so offsets stay non-negative in one table.
         L2D_CUDA_TRY(fit_buf.alloc(3 * kPageBytes));
@@ -403,7 +402,6 @@ int probe_addr_domains_impl(int device, const uint8_t *base, size_t valid_bytes,
         uintptr_t fa = (reinterpret_cast<uintptr_t>(fit_buf.p) + kPageBytes - 1) & ~(uintptr_t)(kPageBytes - 1);
         if (fa < reinterpret_cast<uintptr_t>(base))
             return set_error(L2D_ERR_UNSUPPORTED, "region smaller than one page and below the fit buffer");
-        fit_base = reinterpret_cast<const uint8_t *>(fa);
         fit_shift = fa - reinterpret_cast<uintptr_t>(base);
         fit_pages.push_back(num_pages);  // virtual page index used only for grouping
     }
