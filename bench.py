@@ -109,6 +109,8 @@ class ClockSampler:
         self.samples, self.reasons, self.max_mhz, self.ok = [], 0, None, False
         self.period = period_s
         self._stop = threading.Event()
+        self._t = None
+        self._recording = False
         try:
             import pynvml as N
             N.nvmlInit()
@@ -128,28 +130,41 @@ class ClockSampler:
         except Exception as e:  # noqa: BLE001 -- NVML is optional on the box
             self.err = str(e)
 
-    def _sample(self):
+    def _sample(self, keep=True):
         N = self.N
-        self.samples.append(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM))
-        self.reasons |= int(self._reasons_fn(self.h))
+        mhz = N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)
+        reasons = int(self._reasons_fn(self.h))
+        if keep:
+            self.samples.append(mhz)
+            self.reasons |= reasons
 
     def _run(self):
         while not self._stop.is_set():
             try:
-                self._sample()
+                self._sample(self._recording)
             except Exception:
                 pass
             time.sleep(self.period)
 
-    def __enter__(self):
-        if self.ok:
-            self._sample()
+    def start(self):
+        """Starts sampling without recording, so the thread and NVML are warm before the timed region."""
+        if self.ok and self._t is None:
+            self._recording = False
+            self._sample(False)
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
 
+    def __enter__(self):
+        if self.ok:
+            self.start()
+            self._sample()
+            self._recording = True
+        return self
+
     def __exit__(self, *a):
         if self.ok:
+            self._recording = False
             self._stop.set()
             self._t.join()
             self._sample()
@@ -340,13 +355,14 @@ def run_ours(args, rank, world, local):
     if not rel <= 2e-3:
         raise SystemExit(f"rank {rank}: GEMV self-check failed, rel L2 {rel:.3g}")
 
-    # Headline: K timed steps of the aware GEMV (plus the collectives at N > 1).
+    # Headline: K timed steps of the aware GEMV (plus the exchange at N > 1).  The clock sampler
+    # starts before the warm-up so its thread and NVML are warm when the timed region begins.
+    sampler = ClockSampler(local).start()
     for _ in range(args.warmup):
         step()
     barrier()
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
     with sampler:
         e0.record(stream)
         for i in range(args.steps):
