@@ -24,6 +24,9 @@
  *   l2d_fill_*              applications/gemv/src/gemv_k1024_persistent_subwarp.cu:118-139 (init_data)
  *   l2d_write_smid2side_csv / l2d_read_smid2side_csv   utility/get_smid2side.cu:163-177 file format
  *   l2d_write_mask_csv / l2d_read_mask_csv             utility/get_mask.cu:242-252 file format
+ *   l2d_pool_alloc / l2d_pool_free / l2d_pool_base     utility/sidedgpu.cu:791-882 (cudaMallocSided,
+ *                           cudaFreeSided, cudaGetSidedPoolBase; pool growth :685-745, page
+ *                           classification :187-276)
  */
 #ifndef L2D_H
 #define L2D_H
@@ -247,6 +250,25 @@ L2D_API int l2d_gemv_sharded(l2d_plan *plan, l2d_shard *shard, int mode, void *s
 /* Synchronizes the device, then reads the timeout bits. */
 L2D_API int l2d_shard_status(l2d_shard *shard, uint32_t *status);
 L2D_API int l2d_shard_destroy(l2d_shard *shard);
+
+/* ---- domain-classified memory pool (replaces utility/sidedgpu.cu:791-882: cudaMallocSided,
+ *      cudaFreeSided, cudaGetSidedPoolBase) ----
+ * One pool per device: 64 GiB of virtual addresses, backed 1 GiB at a time (CUDA virtual memory
+ * API); each new chunk is classified by l2d_probe_addr_domains and every 4 KiB granule gets its L2
+ * domain (side).  l2d_pool_alloc hands out ceil(bytes / 4096) free granules of one side as indices
+ * from the pool base (granule g lives at base + g * 4096); cap must hold that many.  Not
+ * thread-safe across processes; thread-safe within one.  Unlike the reference, errors come back as
+ * status codes and a hash finer than 4 KiB is refused (L2D_ERR_UNSUPPORTED). */
+L2D_API int l2d_pool_alloc(int device, size_t bytes, int side, const l2d_probe_opts *opts, uint64_t *granules,
+                           size_t cap, size_t *count);
+L2D_API int l2d_pool_free(int device, const uint64_t *granules, size_t count);
+L2D_API int l2d_pool_base(int device, void **base);
+/* Mapped bytes, free granules per side ([2]) and the pool's mask; any pointer may be NULL. */
+L2D_API int l2d_pool_info(int device, uint64_t *mapped_bytes, uint64_t *free_granules, uint32_t *mask);
+/* The side the pool classified each granule as. */
+L2D_API int l2d_pool_side(int device, const uint64_t *granules, size_t count, int *sides);
+/* Unmaps and frees the whole pool (every granule must be free). */
+L2D_API int l2d_pool_release(int device);
 
 /* ---- helpers used by the benchmark and the CLI ---- */
 /* Reference-mode inputs (init_data): A/x from mix32 of the flat index (stream 0 = A, 1 = x). */

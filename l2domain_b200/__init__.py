@@ -121,6 +121,12 @@ SIGNATURES = {
     "l2d_gemv_sharded": (_i, [_vp, _vp, _i, _vp, _pi]),
     "l2d_shard_status": (_i, [_vp, _pu32]),
     "l2d_shard_destroy": (_i, [_vp]),
+    "l2d_pool_alloc": (_i, [_i, _sz, _i, C.POINTER(ProbeOpts), _pu64, _sz, _psz]),
+    "l2d_pool_free": (_i, [_i, _pu64, _sz]),
+    "l2d_pool_base": (_i, [_i, C.POINTER(_vp)]),
+    "l2d_pool_info": (_i, [_i, _pu64, _pu64, _pu32]),
+    "l2d_pool_side": (_i, [_i, _pu64, _sz, _pi]),
+    "l2d_pool_release": (_i, [_i]),
     "l2d_fill_ref": (_i, [_vp, _i, _u64, _u64, _u32, _i, _i, _vp]),
     "l2d_fill_cfg": (_i, [_vp, _i, _u64, _u64, _u64, _u64, _i, C.c_float, C.c_float, _vp]),
     "l2d_l2_flush": (_i, [_i, _vp]),
@@ -424,6 +430,53 @@ class PeerShard:
 # --------------------------------------------------------------------------------------------
 # Helpers
 # --------------------------------------------------------------------------------------------
+
+# --------------------------------------------------------------------------------------------
+# Domain-classified pool (utility/sidedgpu.cu:791-882 mirrors)
+# --------------------------------------------------------------------------------------------
+
+POOL_GRANULE = 4096
+
+
+def malloc_sided(nbytes: int, side: int, device: int = 0, timeout_ms: int = 0) -> list:
+    """cudaMallocSided: free 4 KiB granules of one L2 side, as indices from :func:`get_sided_pool_base`."""
+    n = max(0, -(-nbytes // POOL_GRANULE))
+    buf = (C.c_uint64 * max(n, 1))()
+    got = C.c_size_t(0)
+    opts = ProbeOpts(timeout_ms=timeout_ms)
+    check(lib().l2d_pool_alloc(device, nbytes, side, C.byref(opts), buf, n, C.byref(got)))
+    return list(buf[: got.value])
+
+
+def free_sided(granules: Sequence[int], device: int = 0) -> None:
+    """cudaFreeSided."""
+    arr = (C.c_uint64 * max(len(granules), 1))(*granules)
+    check(lib().l2d_pool_free(device, arr, len(granules)))
+
+
+def get_sided_pool_base(device: int = 0) -> int:
+    """cudaGetSidedPoolBase: granule g of the pool lives at base + g * 4096."""
+    p = C.c_void_p(0)
+    check(lib().l2d_pool_base(device, C.byref(p)))
+    return int(p.value or 0)
+
+
+def pool_info(device: int = 0) -> dict:
+    mapped, free, mask = C.c_uint64(0), (C.c_uint64 * 2)(), C.c_uint32(0)
+    check(lib().l2d_pool_info(device, C.byref(mapped), free, C.byref(mask)))
+    return {"mapped_bytes": mapped.value, "free_granules": [free[0], free[1]], "mask": mask.value}
+
+
+def pool_sides(granules: Sequence[int], device: int = 0) -> list:
+    arr = (C.c_uint64 * max(len(granules), 1))(*granules)
+    out = (C.c_int * max(len(granules), 1))()
+    check(lib().l2d_pool_side(device, arr, len(granules), out))
+    return list(out[: len(granules)])
+
+
+def pool_release(device: int = 0) -> None:
+    check(lib().l2d_pool_release(device))
+
 
 class _CudaArray:
     """Minimal __cuda_array_interface__ holder, so torch can view library-owned device memory."""

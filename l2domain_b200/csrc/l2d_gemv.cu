@@ -16,10 +16,10 @@
 //    warp, and multiplies with one mixed-precision FMA per element (fma.rn.f32.f16 / .bf16, exact
 //    f16/bf16 -> f32 products) or packed fma.rn.f32x2 for fp32; x sits in shared memory in its
 //    input type, loaded once per CTA.  This keeps the kernel far from the issue limit.
-//  * Per row, each domain group produces one fp32 partial.  Both partials travel inside one packed
-//    64-bit atomicAdd (each half holds ~bits(partial)): the group that sees the other half already
-//    present adds part[0] + part[1] (commutative, so deterministic) and stores y.  No fence, no
-//    second kernel.
+//  * Per row, each domain group stores one fp32 partial (a plain store, no atomic).  The rows are
+//    cut into the intervals where one slot of each group overlaps; the second of the two slots to
+//    finish an interval adds part[0] + part[1] for all its rows (commutative, so deterministic)
+//    and stores y, coalesced.  No second kernel.
 //  * Rows are blocked per slot (one slot per SM) and interleaved over the CTA's warps.  Slots are
 //    claimed with a per-call epoch: a CTA whose SM slot is already taken takes any unclaimed slot,
 //    and the last CTA to finish processes slots nobody claimed, so every row is computed exactly
@@ -70,23 +70,23 @@ struct GemvArgs {
     int64_t spill_num;            // row r is a spill row iff floor((r+1)*num/den) > floor(r*num/den)
     int64_t spill_den;            // (spill rows are taken whole by big_grp; num = 0: no spill rows)
     int big_grp;                  // the group with more SMs
-    unsigned long long *pair;     // [rows_total] packed partial pair, zero between calls
+    float *part;                  // [2][rows_total] each domain group's partial of each row (split calls)
+    unsigned int *meet;           // [n_slots] arrivals per interval of the two groups' slot partitions, zero between calls
     // Peer-memory row sharding (shard_world > 1; batch 1).  Rank 0's first x_slices CTAs push one
-    // slice of x each to every peer; the other ranks' CTAs wait for all slices.  Every final y store
-    // counts its row in a chunk counter; the warp that completes a chunk of 2^chunk_shift rows
-    // pushes it to every peer.  The last CTA waits for every peer's chunks of this step.
+    // slice of x each to every peer; the other ranks' CTAs wait for all slices.  Whoever stores a
+    // row's final y also stores it into every peer's gathered y; each CTA counts the rows it
+    // finished and, at its end, adds the count to every peer's arrival counter for this rank.  The
+    // last CTA waits until every peer's rows of this step have arrived.
     int shard_world;
     int shard_rank;
     unsigned long long shard_epoch;     // step number (1, 2, ...): arrival targets are multiples of it
-    unsigned long long *arrive;         // this rank's arrival counters: [0] x slices, [1 + r] chunks of rank r
+    unsigned long long *arrive;         // this rank's arrival counters: [0] x slices, [1 + r] rows of rank r
     unsigned long long *const *peer_arrive;  // [world] each rank's arrival counters
     uint8_t *const *peer_x;             // [world] each rank's x buffer of this step's parity
     uint8_t *const *peer_y;             // [world] each rank's gathered y buffer of this step's parity
-    const unsigned long long *chunks_of;  // [world] chunk count of each rank's rows
-    unsigned long long *chunk_cnt;      // [chunks of this rank] final-row counters (this rank only)
+    const unsigned long long *rows_of;  // [world] rows of each rank
     int64_t y_shard_off;                // byte offset of this rank's rows in the gathered y
     int64_t x_bytes;
-    int chunk_shift;
     int x_slices;
     uint32_t *shard_status;             // bit 0: x never arrived, bit 1: a peer's rows never arrived
     uint64_t shard_timeout_ns;
@@ -276,153 +276,56 @@ struct RowIter {  // rows_total < 2^31 (checked when the call is set up)
     }
 };
 
-// A row whose pair atomic has been issued by lane 0 but whose returned value is not inspected
-// yet.  It is resolved after the warp has issued the next row's first loads, so the atomic's round
-// trip overlaps with memory traffic instead of stalling the warp.
-struct Pending {
-    unsigned long long old;
-    uint8_t *yp;
-    int64_t row;
-    float sum;
-    int grp;
-    bool active;
-};
-
 __device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Sharded: copies chunk c of this rank's y rows into every peer's gathered y, then counts it in
-// each peer's arrival counter for this rank.  Called by `nthr` threads with ids 0..nthr-1 (a warp,
-// or a single thread); all gathered buffers share one layout, so source and destination have the
-// same alignment.  The rows were stored by other CTAs, which fenced before counting them: the
-// caller saw the count complete, so a fence here and L2 loads (__ldcg) read the final values.
-template <int DT_OUT> __device__ void push_chunk(const GemvArgs &a, int c, int t, int nthr) {
-    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
-    __threadfence();
-    const int64_t r0 = static_cast<int64_t>(c) << a.chunk_shift;
-    const int64_t rows = min(static_cast<int64_t>(1) << a.chunk_shift, a.rows_total - r0);
-    const int64_t off = a.y_shard_off + r0 * eo, bytes = rows * eo;
-    const uint8_t *src = a.peer_y[a.shard_rank] + off;
-    const bool v16 = ((off | bytes) & 15) == 0;
-    for (int p = 0; p < a.shard_world; ++p) {
-        if (p == a.shard_rank) continue;
-        uint8_t *dst = a.peer_y[p] + off;
-        if (v16) {
-            for (int64_t k = t; k < bytes / 16; k += nthr)
-                reinterpret_cast<uint4 *>(dst)[k] = __ldcg(reinterpret_cast<const uint4 *>(src) + k);
-        } else {
-            for (int64_t k = t; k < rows; k += nthr) {
-                if (eo == 4) {
-                    reinterpret_cast<uint32_t *>(dst)[k] = __ldcg(reinterpret_cast<const unsigned int *>(src) + k);
-                } else {
-                    reinterpret_cast<uint16_t *>(dst)[k] = __ldcg(reinterpret_cast<const unsigned short *>(src) + k);
-                }
-            }
-        }
-    }
-    __threadfence_system();
-    if (nthr > 1) __syncwarp();
-    for (int p = t; p < a.shard_world; p += nthr)
-        if (p != a.shard_rank) red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, 1ull);
+// Rows this CTA finished in this launch (sharded kernels count them for the peers' arrival counters).
+__shared__ unsigned int s_fin_rows;
+
+// Sharded, unsplit kernel, lane 0 after storing the final y of a row at yp: the same value into
+// every peer's gathered y (plain stores over NVLink, posted), and one more finished row.
+template <int DT_OUT, bool SH> __device__ __forceinline__ void final_to_peers(const GemvArgs &a, uint8_t *yp, float v) {
+    if (!SH) return;
+    const int64_t off = a.y_shard_off + (yp - a.y);
+    for (int p = 0; p < a.shard_world; ++p)
+        if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + off, v);
+    atomicAdd_block(&s_fin_rows, 1u);
 }
 
-// Spill rows in [lo, hi): the spill predicate telescopes, floor(hi num/den) - floor(lo num/den).
-__device__ __forceinline__ int64_t spills_in(const GemvArgs &a, int64_t lo, int64_t hi) {
-    return hi * a.spill_num / a.spill_den - lo * a.spill_num / a.spill_den;
-}
-
-// Sharded, the whole CTA at the end of a slot [r0, r1) whose rows are all visited and whose last
-// deferred row is resolved (every warp fenced its y stores, then a CTA barrier).  Row r of a split
-// call is final once both groups visited it (spill rows: once the bigger group did), so chunk c is
-// final when the visits counted into chunk_cnt[c] reach 2 rows(c) - spills(c) per step (rows(c)
-// unsplit).  Each slot adds its visits per chunk in closed form; the CTA that completes a chunk
-// pushes it to the peers.
-// The slot's row range and group role are read back from shared memory (s_slot_info, written when
-// the slot started) so they need no registers during the row loop.
-__shared__ long long s_slot_info[3];  // r0, r1, small group
-
-template <int DT_OUT, bool SPLIT>
-__device__ __forceinline__ void shard_count_slot(const GemvArgs &a, int warp, int nwarps, int lane) {
-    __shared__ int s_n;
-    __shared__ int s_done[64];
-    if (threadIdx.x == 0) s_n = 0;
-    __syncthreads();
-    const int64_t r0 = s_slot_info[0], r1 = s_slot_info[1];
-    const bool small_grp = s_slot_info[2] != 0;
-    const int64_t cs = static_cast<int64_t>(1) << a.chunk_shift;
-    const int64_t c_first = r0 >> a.chunk_shift, c_last = (r1 - 1) >> a.chunk_shift;
-    for (int64_t c = c_first + threadIdx.x; c <= c_last; c += blockDim.x) {
-        const int64_t cr0 = c * cs, cr1 = min(cr0 + cs, a.rows_total);
-        const int64_t lo = max(r0, cr0), hi = min(r1, cr1);
-        const int64_t visits = (hi - lo) - (small_grp ? spills_in(a, lo, hi) : 0);
-        const int64_t expect = SPLIT ? 2 * (cr1 - cr0) - spills_in(a, cr0, cr1) : (cr1 - cr0);
-        if (visits <= 0) continue;
-        const unsigned long long old = atomicAdd(a.chunk_cnt + c, static_cast<unsigned long long>(visits));
-        if (old + static_cast<unsigned long long>(visits) == a.shard_epoch * static_cast<unsigned long long>(expect)) {
-            const int k = atomicAdd(&s_n, 1);
-            if (k < 64) s_done[k] = static_cast<int>(c);
-        }
-    }
-    __syncthreads();
-    const int n = min(s_n, 64);
-    for (int k = warp; k < n; k += nwarps) push_chunk<DT_OUT>(a, s_done[k], lane, 32);
-    __syncthreads();
-}
-
-// Returns true when it stored the final y of row p.row.
-template <int DT_OUT> __device__ __forceinline__ bool resolve(const GemvArgs &a, Pending &p) {
-    if (!p.active) return false;
-    p.active = false;
-    const uint32_t other = static_cast<uint32_t>(p.old >> (32 * (p.grp ^ 1)));
-    if (other != 0u) {
-        store_out<DT_OUT>(p.yp, p.sum + __uint_as_float(~other));  // commutative: same bits either way
-        a.pair[p.row] = 0ull;
-        return true;
-    }
-    return false;
-}
-
-// One row of A for one domain group.  SPLIT: the row is shared by both groups (false for the
-// unsplit kernel and for spill rows, which the bigger group takes whole).
-template <int DT_IN, int DT_OUT>
-__device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool SPLIT, int grp, int lane,
-                                         const uint8_t *xs, int64_t xs_b0, Pending &pend) {
+// One row of A for one domain group.  SPLITK: the split kernel (both groups visit every row and
+// store partials); split_row: this row's units are divided between the groups (false for the
+// spill rows, which the bigger group takes whole).  The unsplit kernel stores y directly.
+template <int DT_IN, int DT_OUT, bool SPLITK, bool SH>
+__device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, bool split_row, int grp, int lane,
+                                         const uint8_t *xs, int64_t xs_b0) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
     constexpr int eb = DT_IN == L2D_F32 ? 4 : 2;
     const int64_t row = it.row, b = it.b, i = it.i;
     const uint8_t *rowp = a.A + b * a.stride_a_bytes + i * a.lda_bytes;
     const bool xsm = xs != nullptr;
     const uint8_t *xrow = xsm ? xs + (b - xs_b0) * ((a.row_bytes + 15) & ~int64_t(15)) : a.x + b * a.stride_x_bytes;
-    uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
     const uint64_t rs = static_cast<uint64_t>(rowp - a.region_base);
     const uint64_t re = rs + static_cast<uint64_t>(a.row_bytes);
     const uint64_t u0 = rs >> kUnitShift;
     const uint64_t u1 = (re + (1u << kUnitShift) - 1) >> kUnitShift;
-    if (u0 == u1) {  // N == 0: y = 0, written once
-        if (lane == 0 && grp == 0) store_out<DT_OUT>(yp, 0.0f);
-        return;
-    }
     const uint8_t *abase = a.region_base + lane * 32;
     const int64_t xoff0 = static_cast<int64_t>(lane) * 32 - static_cast<int64_t>(rs);
     Acc<DT_IN> acc;
-    bool saw_mine = false, saw_other = false, resolved = false;
-    for (uint64_t ub = u0; ub < u1; ub += 64) {
+    for (uint64_t ub = u0; ub < u1; ub += 64) {  // no iteration when N == 0: the row's sum is 0
         const uint64_t ua = ub + lane, uc = ub + 32 + lane;
         const bool ina = ua < u1, inc = uc < u1;
         const bool fa = ina && (ua << kUnitShift) >= rs && ((ua + 1) << kUnitShift) <= re;
         const bool fc = inc && (uc << kUnitShift) >= rs && ((uc + 1) << kUnitShift) <= re;
         bool ma = ina, mc = inc;
-        if (SPLIT) {
+        if (split_row) {
             ma = ina && unit_dom(a, ua) == grp;
             mc = inc && unit_dom(a, uc) == grp;
-            saw_other |= __any_sync(0xffffffffu, (ina && !ma) || (inc && !mc));
         }
         uint64_t full = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && fa)) |
                         (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && fc)) << 32);
         uint64_t edge = static_cast<uint64_t>(__ballot_sync(0xffffffffu, ma && !fa)) |
                               (static_cast<uint64_t>(__ballot_sync(0xffffffffu, mc && !fc)) << 32);
-        saw_mine |= (full | edge) != 0ull;
         while (full) {
             int idx[kUnroll];
 #pragma unroll
@@ -434,10 +337,6 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u)
                 if (idx[u] >= 0) av[u] = ld_stream32(abase + ((ub + idx[u]) << kUnitShift));
-            if (!resolved) {
-                if (lane == 0) resolve<DT_OUT>(a, pend);
-                resolved = true;
-            }
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
                 if (idx[u] >= 0) {
@@ -460,21 +359,91 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     float sum = acc.total();
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane != 0 || !saw_mine) return;
-    if (!SPLIT || !saw_other) {
+    if (lane != 0) return;
+    if (SPLITK) {
+        // The group's partial (0 when the row has no units in its domain).  A spill row is whole
+        // here, so the other group's partial is 0.
+        a.part[grp * a.rows_total + row] = sum;
+        if (!split_row) a.part[(grp ^ 1) * a.rows_total + row] = 0.0f;
+    } else {
+        uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
         store_out<DT_OUT>(yp, sum);
-        return;
+        final_to_peers<DT_OUT, SH>(a, yp, sum);
     }
-    // Both domain groups own part of this row.  Each adds ~bits(partial) into its own 32-bit half
-    // of the row's pair word; ~bits is never 0 for a value arithmetic produces, so the group that
-    // finds the other half non-zero holds both partials and finishes the row (in resolve()).
-    if (!resolved) resolve<DT_OUT>(a, pend);
-    pend.old = atomicAdd(a.pair + row, static_cast<unsigned long long>(~__float_as_uint(sum)) << (32 * grp));
-    pend.yp = yp;
-    pend.row = row;
-    pend.sum = sum;
-    pend.grp = grp;
-    pend.active = true;
+}
+
+// Split kernel, the whole CTA once its slot (group grp, rows [r0, r1)) has stored every partial and
+// every warp has fenced: for each slot j of the other group that overlaps [r0, r1), the interval
+// of the two slots counts one arrival.  Interval (i0, i1) -- slot i0 of group 0 with slot i1 of
+// group 1 -- is number i0 + i1 of the merged partition, so meet[] needs n_dom0 + n_dom1 entries.
+// The second arrival holds both partials of every row of the interval: it stores y = part0 + part1
+// (and, sharded, the same into every peer's gathered y) and clears the counter for the next call.
+// Element offset of global row r (problem r / M, row r % M) in y.
+__device__ __forceinline__ int64_t y_index(const GemvArgs &a, int64_t r) {
+    if (a.rows_total == a.M) return r;
+    const int64_t b = r / a.M;
+    return b * a.stride_y_elems + (r - b * a.M);
+}
+
+template <int DT_OUT, bool SH>
+__device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int idx, int64_t r0, int64_t r1) {
+    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    constexpr int kMaxIv = 32;
+    __shared__ int s_n;
+    __shared__ long long s_lo[kMaxIv], s_hi[kMaxIv];
+    __shared__ int s_id[kMaxIv];
+    if (threadIdx.x == 0) s_n = 0;
+    __syncthreads();
+    const int n_other = grp ? a.n_dom0 : a.n_dom1;
+    for (int j = threadIdx.x; j < n_other; j += blockDim.x) {
+        const int64_t o0 = a.rows_total * j / n_other, o1 = a.rows_total * (j + 1) / n_other;
+        const int64_t lo = max(r0, o0), hi = min(r1, o1);
+        if (lo >= hi) continue;
+        const int id = idx + j;
+        if (atomicAdd(a.meet + id, 1u) == 1u) {
+            const int k = atomicAdd(&s_n, 1);
+            if (k < kMaxIv) {
+                s_lo[k] = lo;
+                s_hi[k] = hi;
+                s_id[k] = id;
+            } else {
+                // More overlapping slots than the list holds (only with very unequal groups):
+                // combine right here, one thread for the interval.
+                __threadfence();
+                for (int64_t r = lo; r < hi; ++r) {
+                    const float v = __ldcg(a.part + r) + __ldcg(a.part + a.rows_total + r);
+                    const int64_t yi = y_index(a, r);
+                    store_out<DT_OUT>(a.y + yi * eo, v);
+                    if (SH)
+                        for (int p = 0; p < a.shard_world; ++p)
+                            if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
+                }
+                if (SH) atomicAdd_block(&s_fin_rows, static_cast<unsigned int>(hi - lo));
+                a.meet[id] = 0u;
+            }
+        }
+    }
+    __syncthreads();
+    const int n = min(s_n, kMaxIv);
+    if (n == 0) return;
+    __threadfence();  // the other group's partials, counted before its arrival
+    for (int k = 0; k < n; ++k) {
+        const int64_t lo = s_lo[k], hi = s_hi[k];
+        for (int64_t r = lo + threadIdx.x; r < hi; r += blockDim.x) {
+            const float v = __ldcg(a.part + r) + __ldcg(a.part + a.rows_total + r);
+            const int64_t yi = y_index(a, r);
+            store_out<DT_OUT>(a.y + yi * eo, v);
+            if (SH)
+                for (int p = 0; p < a.shard_world; ++p)
+                    if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
+        }
+        if (threadIdx.x == 0) {
+            a.meet[s_id[k]] = 0u;
+            if (SH) atomicAdd_block(&s_fin_rows, static_cast<unsigned int>(hi - lo));
+        }
+    }
+    if (SH) __threadfence_system();  // the peer copies before the CTA's count at its end
+    __syncthreads();
 }
 
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
@@ -494,15 +463,8 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
         b0 = r0 / a.M;
         xs = stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
     }
-    Pending pend;
-    pend.active = false;
     // The smaller domain group skips the spill rows, which the bigger group takes whole.
     const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
-    if (SH && threadIdx.x == 0) {
-        s_slot_info[0] = r0;
-        s_slot_info[1] = r1;
-        s_slot_info[2] = small_grp;
-    }
     const int32_t step_phase =
         a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
     RowIter it;
@@ -510,14 +472,21 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     for (int64_t row = r0 + warp; row < r1; row += nwarps, it.advance(a, nwarps, step_phase)) {
         const bool spill = SPLIT && it.spill(a);
         if (spill && small_grp) continue;
-        gemv_row<DT_IN, DT_OUT>(a, it, SPLIT && !spill, grp, lane, xs, b0, pend);
+        gemv_row<DT_IN, DT_OUT, SPLIT, SH>(a, it, SPLIT && !spill, grp, lane, xs, b0);
     }
     if (lane == 0) {
-        resolve<DT_OUT>(a, pend);
-        __threadfence();  // this warp's y stores are visible before the CTA reports done
+        if (SH && !SPLIT) {
+            __threadfence_system();  // the peer copies of this warp's rows before the CTA's count
+        } else {
+            __threadfence();  // this warp's partials (or y) before the slot's arrival / the CTA's done count
+        }
     }
-    if (SH) shard_count_slot<DT_OUT, SPLIT>(a, warp, nwarps, lane);
-    if (a.x_smem) __syncthreads();  // the staged x may be replaced for the next slot
+    if (SPLIT) {
+        __syncthreads();
+        meet_and_combine<DT_OUT, SH>(a, grp, idx, r0, r1);
+    } else if (a.x_smem) {
+        __syncthreads();  // the staged x may be replaced for the next slot
+    }
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
@@ -560,12 +529,22 @@ template <bool SH> __device__ __forceinline__ void shard_prologue(const GemvArgs
     __syncwarp();
 }
 
-// Sharded epilogue (last CTA): wait (bounded) until every peer's chunks of this step have arrived.
+// Sharded, every CTA at its end (after a barrier that follows every warp's system-scope fence):
+// this CTA's finished rows are added to every peer's arrival counter for this rank.
+template <bool SH> __device__ __forceinline__ void shard_signal(const GemvArgs &a) {
+    if (!SH) return;
+    const int p = threadIdx.x;
+    const unsigned int n = s_fin_rows;
+    if (p < a.shard_world && p != a.shard_rank && n != 0u)
+        red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, static_cast<unsigned long long>(n));
+}
+
+// Sharded epilogue (last CTA): wait (bounded) until every peer's rows of this step have arrived.
 template <bool SH> __device__ __forceinline__ void shard_final_wait(const GemvArgs &a) {
     if (!SH) return;
     const int p = threadIdx.x;
     if (p < a.shard_world && p != a.shard_rank) {
-        const unsigned long long want = a.shard_epoch * a.chunks_of[p];
+        const unsigned long long want = a.shard_epoch * a.rows_of[p];
         const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
         while (ld_acquire_sys(a.arrive + 1 + p) < want) {
             if (dev::globaltimer_ns() > deadline) {
@@ -626,6 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
             s_slot = got;
             s_epoch = E;
             s_count = 0;
+            if (SH) s_fin_rows = 0u;
         }
         shard_prologue<SH>(a, lane);
     }
@@ -639,7 +619,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         if (s_last) __threadfence();  // acquire side: the other CTAs' y rows before the epilogue
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        shard_signal<SH>(a);
+        return;
+    }
     // Last CTA: slots whose SM never hosted a CTA of this launch, found by one parallel sweep.
     const unsigned long long E = s_epoch;
     for (int t = tid; t < a.n_slots; t += blockDim.x) {
@@ -652,6 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
         __syncthreads();
     }
+    shard_signal<SH>(a);
     shard_final_wait<SH>(a);
     if (tid == 0) {
         a.ctl[1] = 0ull;
@@ -719,6 +703,9 @@ namespace {
 std::mutex g_sm_cache_mu;
 std::map<int, std::vector<int>> g_sm_cache;  // device -> SM domain map
 
+}  // namespace
+
+// SM -> domain map of a device, probed once per process.
 int cached_sm_map(int device, std::vector<int> &out) {
     {
         std::lock_guard<std::mutex> lk(g_sm_cache_mu);
@@ -739,6 +726,8 @@ int cached_sm_map(int device, std::vector<int> &out) {
     out = map;
     return L2D_OK;
 }
+
+namespace {
 
 // Allocation containing p, through the driver entry point (no link-time libcuda dependency).
 typedef int (*PFN_memGetAddressRange)(unsigned long long *, size_t *, unsigned long long);
@@ -786,7 +775,8 @@ struct l2d_plan {
     size_t dev_bytes = 0;
     int32_t *d_sm_slot = nullptr;
     uint32_t *d_attr_bits = nullptr;
-    unsigned long long *d_pair = nullptr;
+    float *d_part = nullptr;
+    unsigned int *d_meet = nullptr;
     size_t x_smem_bytes = 0;  // dynamic shared memory holding the x vectors (0 = read x through L1)
     unsigned long long *d_claim = nullptr;
     unsigned long long *d_ctl = nullptr;
@@ -963,8 +953,10 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
     off = align256(off + 4 * sizeof(unsigned long long));
     const size_t o_claim = off;
     off = align256(off + static_cast<size_t>(p->n_slots) * sizeof(unsigned long long));
-    const size_t o_pair = off;
-    off = align256(off + R * sizeof(unsigned long long));
+    const size_t o_meet = off;
+    off = align256(off + static_cast<size_t>(p->n_slots) * sizeof(unsigned int));
+    const size_t o_part = off;
+    off = align256(off + 2 * R * sizeof(float));
     p->dev_bytes = off;
     cudaError_t e = cudaMalloc(&p->dev_block, off);
     if (e != cudaSuccess) {
@@ -976,7 +968,8 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
     p->d_attr_bits = reinterpret_cast<uint32_t *>(blk + o_attr);
     p->d_ctl = reinterpret_cast<unsigned long long *>(blk + o_ctl);
     p->d_claim = reinterpret_cast<unsigned long long *>(blk + o_claim);
-    p->d_pair = reinterpret_cast<unsigned long long *>(blk + o_pair);
+    p->d_meet = reinterpret_cast<unsigned int *>(blk + o_meet);
+    p->d_part = reinterpret_cast<float *>(blk + o_part);
     e = cudaMemset(p->dev_block, 0, off);
     if (e == cudaSuccess) e = cudaMemcpy(p->d_sm_slot, slot.data(), kMaxSmid * sizeof(int32_t), cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
@@ -1060,7 +1053,8 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.n_slots = p->n_slots;
     a.n_dom0 = p->n_dom[0];
     a.n_dom1 = p->n_dom[1];
-    a.pair = p->d_pair;
+    a.part = p->d_part;
+    a.meet = p->d_meet;
     a.claim = p->d_claim;
     a.ctl = p->d_ctl;
     a.x_smem = p->x_smem_bytes > 0;
@@ -1082,11 +1076,11 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
 // Host-side guard before a launch: every pointer the kernel dereferences unconditionally must be set
 // (a call that reaches the kernel with a missing scratch pointer is refused, never launched).
 int check_args(const GemvArgs &a) {
-    if (!a.x || !a.y || !a.sm_slot || !a.pair || !a.claim || !a.ctl || a.n_slots <= 0 ||
+    if (!a.x || !a.y || !a.sm_slot || !a.part || !a.meet || !a.claim || !a.ctl || a.n_slots <= 0 ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
-    if (a.shard_world > 1 && (!a.arrive || !a.peer_arrive || !a.peer_x || !a.peer_y || !a.chunks_of ||
-                              !a.chunk_cnt || !a.shard_status || a.x_slices <= 0))
+    if (a.shard_world > 1 && (!a.arrive || !a.peer_arrive || !a.peer_x || !a.peer_y || !a.rows_of ||
+                              !a.shard_status || a.x_slices <= 0))
         return set_error(L2D_ERR_INVALID, "sharded gemv arguments incomplete (internal error)");
     return L2D_OK;
 }
@@ -1120,11 +1114,9 @@ int shard_fill_args(GemvArgs *a, const ShardArgs &sh) {
     a->peer_arrive = sh.peer_arrive;
     a->peer_x = sh.peer_x;
     a->peer_y = sh.peer_y;
-    a->chunks_of = sh.chunks_of;
-    a->chunk_cnt = sh.chunk_cnt;
+    a->rows_of = sh.rows_of;
     a->y_shard_off = sh.y_shard_off;
     a->x_bytes = sh.x_bytes;
-    a->chunk_shift = sh.chunk_shift;
     a->x_slices = sh.x_slices;
     a->shard_status = sh.status;
     a->shard_timeout_ns = sh.timeout_ns;
@@ -1197,10 +1189,11 @@ int l2d_plan_domain_map(const l2d_plan *p, int *sm_domain, int cap, int *num_sm,
 // cudaStreamBeginCapture and cudaStreamEndCapture (a cudaMalloc there breaks the capture), or a
 // latency-critical path that must not enter the allocator.  l2d_gemv_noalloc runs the same kernel
 // as l2d_gemv without a plan: its scratch (control words, slot claims, the SM->slot table, the
-// attr bits and one pair word per row) lives in the file-scope array below, which every GPU that
-// loads this library holds until the process exits.  Limits: L2D_NOALLOC_MAX_ROWS rows over all
-// problems, L2D_NOALLOC_MAX_PAGES 2 MiB pages of A.  Every call shares the array and leaves its
-// contents for the next call (the pair words return to zero when a call completes), so calls
+// attr bits, the interval counters and two partials per row) lives in the file-scope array below,
+// which every GPU that loads this library holds until the process exits.  Limits:
+// L2D_NOALLOC_MAX_ROWS rows over all problems, L2D_NOALLOC_MAX_PAGES 2 MiB pages of A.  Every call
+// shares the array and leaves its contents for the next call (the interval counters return to zero
+// when a call completes), so calls
 // that overlap on the GPU (other streams, other threads) race and must be serialised by the
 // caller.
 // ---------------------------------------------------------------------------------------------
@@ -1210,10 +1203,11 @@ namespace noalloc {
 
 constexpr size_t kCtlOff = 0;
 constexpr size_t kClaimOff = 256;
-constexpr size_t kSlotOff = kClaimOff + kMaxSmid * sizeof(unsigned long long);
+constexpr size_t kMeetOff = kClaimOff + kMaxSmid * sizeof(unsigned long long);
+constexpr size_t kSlotOff = kMeetOff + kMaxSmid * sizeof(unsigned int);
 constexpr size_t kAttrOff = kSlotOff + kMaxSmid * sizeof(int32_t);
-constexpr size_t kPairOff = kAttrOff + (L2D_NOALLOC_MAX_PAGES / 32) * sizeof(uint32_t);
-constexpr size_t kBytes = kPairOff + static_cast<size_t>(L2D_NOALLOC_MAX_ROWS) * sizeof(unsigned long long);
+constexpr size_t kPartOff = kAttrOff + (L2D_NOALLOC_MAX_PAGES / 32) * sizeof(uint32_t);
+constexpr size_t kBytes = kPartOff + 2 * static_cast<size_t>(L2D_NOALLOC_MAX_ROWS) * sizeof(float);
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_scratch[kBytes];
@@ -1356,7 +1350,8 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
     a.n_slots = num_sm;
     a.n_dom0 = n_dom[0];
     a.n_dom1 = n_dom[1];
-    a.pair = reinterpret_cast<unsigned long long *>(scratch + noalloc::kPairOff);
+    a.part = reinterpret_cast<float *>(scratch + noalloc::kPartOff);
+    a.meet = reinterpret_cast<unsigned int *>(scratch + noalloc::kMeetOff);
     a.claim = reinterpret_cast<unsigned long long *>(scratch + noalloc::kClaimOff);
     a.ctl = reinterpret_cast<unsigned long long *>(scratch + noalloc::kCtlOff);
     a.big_grp = n_dom[1] > n_dom[0] ? 1 : 0;

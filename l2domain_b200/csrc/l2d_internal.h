@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <vector>
 
 namespace l2d {
 
@@ -30,6 +31,9 @@ inline int parity_domain(uint32_t mask, uint64_t addr, int attr) {
 
 inline int lowest_bit_or(uint32_t mask, int fallback) { return mask ? __builtin_ctz(mask) : fallback; }
 
+// SM -> domain map of a device, probed once per process (l2d_gemv.cu).
+int cached_sm_map(int device, std::vector<int> &out);
+
 // Peer-memory sharding fields of one l2d_gemv_sharded step (device pointers unless noted).
 struct ShardArgs {
     int world, rank;
@@ -38,10 +42,9 @@ struct ShardArgs {
     unsigned long long *const *peer_arrive;
     uint8_t *const *peer_x;
     uint8_t *const *peer_y;
-    const unsigned long long *chunks_of;
-    unsigned long long *chunk_cnt;
+    const unsigned long long *rows_of;
     int64_t y_shard_off, x_bytes;
-    int chunk_shift, x_slices;
+    int x_slices;
     uint32_t *status;
     uint64_t timeout_ns;
 };

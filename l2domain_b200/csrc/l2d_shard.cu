@@ -7,11 +7,11 @@
 //   * rank 0's first kXSlices CTAs each push one slice of x into every peer's x buffer and count it
 //     in that peer's x arrival counter (system-scope release); the other ranks' CTAs wait for all
 //     slices before they stage x;
-//   * when a CTA finishes a slot (a block of rows for one L2-domain group), it adds its row visits
-//     to the counters of the chunks the slot overlaps; the CTA that completes a chunk (at most
-//     kMaxChunks per rank) pushes its rows into every peer's gathered y and counts the chunk there,
-//     so the gather runs under the GEMV as slots finish;
-//   * the last CTA waits until every peer's chunks of the step have arrived.
+//   * whoever stores a row's final y (the domain group that finishes the row) also stores it into
+//     every peer's gathered y, so the gather runs under the GEMV as rows finish; each CTA counts
+//     the rows it finished and, after a system-scope fence, adds the count to every peer's arrival
+//     counter for this rank;
+//   * the last CTA waits until every peer's rows of the step have arrived.
 // x and y are double-buffered by the parity of the step number, so a step never overwrites data a
 // peer may still read from the step before (a rank enters step e+1 only after every peer's step-e
 // rows arrived, i.e. after every peer finished reading step e-1's buffers).  Arrival counters only
@@ -45,15 +45,13 @@ namespace shard {
 constexpr uint32_t kMagic = 0x4c32445du;  // "L2D]"
 constexpr uint32_t kVersion = 2;
 constexpr int kMaxWorld = 64;
-constexpr int kMinChunkShift = 9;  // at least 512 rows per pushed chunk
-constexpr int kMaxChunks = 64;     // at most this many chunks per rank (the kernel's per-slot list)
 constexpr int kXSlices = 32;    // x is pushed in this many slices, one per CTA of rank 0
 
 struct Blob {
     uint32_t magic, version;
     int32_t pid, rank, world, device;
     int64_t bytes, rows;
-    int32_t chunk_shift, x_slices;
+    int32_t x_slices, reserved;
     uint64_t raw;  // device address in the exporting process (used when importer == exporter)
     cudaIpcMemHandle_t handle;
 };
@@ -69,7 +67,7 @@ __device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsig
 }
 
 // The step of a rank without rows (M_total < world): rank 0 still pushes x (kXSlices CTAs of one
-// warp, as the GEMV prologue does), and CTA 0 waits for the peers' chunks.
+// warp, as the GEMV prologue does), and CTA 0 waits for the peers' rows.
 __global__ void k_shard_idle(ShardArgs sh, const uint8_t *x) {
     const int lane = threadIdx.x;
     if (sh.rank == 0 && sh.world > 1) {
@@ -89,7 +87,7 @@ __global__ void k_shard_idle(ShardArgs sh, const uint8_t *x) {
     if (blockIdx.x != 0) return;
     for (int p = lane; p < sh.world; p += 32) {
         if (p == sh.rank) continue;
-        const unsigned long long want = sh.epoch * sh.chunks_of[p];
+        const unsigned long long want = sh.epoch * sh.rows_of[p];
         const uint64_t deadline = dev::globaltimer_ns() + sh.timeout_ns;
         while (ld_acquire_sys(sh.arrive + 1 + p) < want) {
             if (dev::globaltimer_ns() > deadline) {
@@ -117,11 +115,9 @@ struct l2d_shard {
     std::vector<uint8_t *> peer;  // [world] peer bases in this process's address space
     std::vector<bool> opened;     // opened through IPC (closed on destroy)
     // Local device tables: peer_x[2][world], peer_y[2][world], peer_arrive[world] (pointers),
-    // chunks_of[world] (u64), status (u32, padded to 16 bytes), chunk_cnt[own chunks] (u64).
+    // rows_of[world] (u64), status (u32).
     uint8_t *tables = nullptr;
-    size_t off_chunks_of = 0, off_status = 0, off_cnt = 0, tables_bytes = 0;
-    int64_t own_chunks = 0;
-    int chunk_shift = 9;
+    size_t off_rows_of = 0, off_status = 0, tables_bytes = 0;
     bool connected = false;
     unsigned long long epoch = 0;
 };
@@ -135,18 +131,10 @@ uint8_t **tab_y(l2d_shard *s, int par) { return reinterpret_cast<uint8_t **>(s->
 unsigned long long **tab_arrive(l2d_shard *s) {
     return reinterpret_cast<unsigned long long **>(s->tables) + 4 * s->world;
 }
-unsigned long long *tab_chunks_of(l2d_shard *s) {
-    return reinterpret_cast<unsigned long long *>(s->tables + s->off_chunks_of);
+unsigned long long *tab_rows_of(l2d_shard *s) {
+    return reinterpret_cast<unsigned long long *>(s->tables + s->off_rows_of);
 }
 uint32_t *status_word(l2d_shard *s) { return reinterpret_cast<uint32_t *>(s->tables + s->off_status); }
-unsigned long long *chunk_counters(l2d_shard *s) { return reinterpret_cast<unsigned long long *>(s->tables + s->off_cnt); }
-
-int chunk_shift_for(int64_t rows) {
-    int sh = shard::kMinChunkShift;
-    while (((rows + (int64_t(1) << sh) - 1) >> sh) > shard::kMaxChunks) ++sh;
-    return sh;
-}
-int64_t chunks_for(int64_t rows, int sh) { return (rows + (int64_t(1) << sh) - 1) >> sh; }
 
 struct DeviceScope {
     int prev = -1;
@@ -169,11 +157,9 @@ ShardArgs shard_args(l2d_shard *s, int par, unsigned long long e) {
     sh.peer_arrive = tab_arrive(s);
     sh.peer_x = tab_x(s, par);
     sh.peer_y = tab_y(s, par);
-    sh.chunks_of = tab_chunks_of(s);
-    sh.chunk_cnt = chunk_counters(s);
+    sh.rows_of = tab_rows_of(s);
     sh.y_shard_off = s->row0 * s->eb_out;
     sh.x_bytes = s->N * s->eb_in;
-    sh.chunk_shift = s->chunk_shift;
     sh.x_slices = shard::kXSlices;
     sh.status = status_word(s);
     sh.timeout_ns = s->timeout_ns;
@@ -224,12 +210,9 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(M_total, 1)) * s->eb_out);
     }
     s->bytes = off;
-    s->chunk_shift = chunk_shift_for(rows);
-    s->own_chunks = chunks_for(rows, s->chunk_shift);
-    s->off_chunks_of = 5 * world * sizeof(void *);
-    s->off_status = s->off_chunks_of + world * sizeof(unsigned long long);
-    s->off_cnt = s->off_status + 16;
-    s->tables_bytes = s->off_cnt + std::max<int64_t>(s->own_chunks, 1) * sizeof(unsigned long long);
+    s->off_rows_of = 5 * world * sizeof(void *);
+    s->off_status = s->off_rows_of + world * sizeof(unsigned long long);
+    s->tables_bytes = s->off_status + 16;
     cudaError_t e = cudaMalloc(&s->base, s->bytes);
     if (e == cudaSuccess) e = cudaMemset(s->base, 0, s->bytes);
     if (e == cudaSuccess) e = cudaMalloc(&s->tables, s->tables_bytes);
@@ -265,7 +248,6 @@ int l2d_shard_handle(const l2d_shard *s, void *blob, size_t cap, size_t *len) {
     b.device = s->device;
     b.bytes = static_cast<int64_t>(s->bytes);
     b.rows = s->rows;
-    b.chunk_shift = s->chunk_shift;
     b.x_slices = shard::kXSlices;
     b.raw = reinterpret_cast<uint64_t>(s->base);
     L2D_CUDA_TRY(cudaIpcGetMemHandle(&b.handle, s->base));
@@ -280,16 +262,15 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
                          sizeof(shard::Blob));
     DeviceScope scope(s->device);
     const pid_t me = getpid();
-    std::vector<unsigned long long> chunks(s->world, 0);
+    std::vector<unsigned long long> rows_of(s->world, 0);
     int64_t rows_sum = 0;
     for (int r = 0; r < s->world; ++r) {
         shard::Blob b;
         std::memcpy(&b, static_cast<const uint8_t *>(blobs) + r * blob_len, sizeof b);
         if (b.magic != shard::kMagic || b.version != shard::kVersion || b.rank != r || b.world != s->world ||
-            b.bytes != static_cast<int64_t>(s->bytes) || b.chunk_shift < shard::kMinChunkShift ||
-            b.chunk_shift > 40 || b.x_slices != shard::kXSlices || b.rows < 0)
+            b.bytes != static_cast<int64_t>(s->bytes) || b.x_slices != shard::kXSlices || b.rows < 0)
             return set_error(L2D_ERR_INVALID, "shard blob %d does not match this shard layout", r);
-        chunks[r] = static_cast<unsigned long long>(chunks_for(b.rows, b.chunk_shift));
+        rows_of[r] = static_cast<unsigned long long>(b.rows);
         rows_sum += b.rows;
         if (r == s->rank || s->peer[r]) continue;
         if (b.pid == static_cast<int32_t>(me)) {
@@ -314,7 +295,7 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
         }
     for (int r = 0; r < s->world; ++r) host[4 * s->world + r] = s->peer[r] + s->off_arrive;
     L2D_CUDA_TRY(cudaMemcpy(s->tables, host.data(), host.size() * sizeof(void *), cudaMemcpyHostToDevice));
-    L2D_CUDA_TRY(cudaMemcpy(tab_chunks_of(s), chunks.data(), chunks.size() * sizeof(unsigned long long),
+    L2D_CUDA_TRY(cudaMemcpy(tab_rows_of(s), rows_of.data(), rows_of.size() * sizeof(unsigned long long),
                             cudaMemcpyHostToDevice));
     s->connected = true;
     return L2D_OK;
