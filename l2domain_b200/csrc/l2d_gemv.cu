@@ -72,22 +72,22 @@ struct GemvArgs {
     int big_grp;                  // the group with more SMs
     float *part;                  // [2][rows_total] each domain group's partial of each row (split calls)
     unsigned int *meet;           // [n_slots] arrivals per interval of the two groups' slot partitions, zero between calls
-    // Peer-memory row sharding (shard_world > 1; batch 1).  Rank 0's first x_slices CTAs push one
-    // slice of x each to every peer; the other ranks' CTAs wait for all slices.  Whoever stores a
-    // row's final y also stores it into every peer's gathered y; each CTA counts the rows it
-    // finished and, at its end, adds the count to every peer's arrival counter for this rank.  The
-    // last CTA waits until every peer's rows of this step have arrived.
+    // Peer-memory row sharding (shard_world > 1; batch 1).  Rank 0's CTAs push x to every peer as
+    // flagged 8-byte words (4 bytes of x, the step number), which the other ranks' CTAs check while
+    // they stage x: no fence and no counter on the way in.  Whoever stores a row's final y also
+    // stores it into every peer's gathered y and fences at system scope before its CTA reports
+    // done; the last CTA adds the rank's rows to every peer's arrival counter for this rank, then
+    // waits until every peer's rows of this step have arrived.
     int shard_world;
     int shard_rank;
     unsigned long long shard_epoch;     // step number (1, 2, ...): arrival targets are multiples of it
-    unsigned long long *arrive;         // this rank's arrival counters: [0] x slices, [1 + r] rows of rank r
+    unsigned long long *arrive;         // this rank's arrival counters: [1 + r] rows of rank r
     unsigned long long *const *peer_arrive;  // [world] each rank's arrival counters
-    uint8_t *const *peer_x;             // [world] each rank's x buffer of this step's parity
+    uint2 *const *peer_xw;              // [world] each rank's flagged-word x buffer of this step's parity
     uint8_t *const *peer_y;             // [world] each rank's gathered y buffer of this step's parity
     const unsigned long long *rows_of;  // [world] rows of each rank
     int64_t y_shard_off;                // byte offset of this rank's rows in the gathered y
     int64_t x_bytes;
-    int x_slices;
     uint32_t *shard_status;             // bit 0: x never arrived, bit 1: a peer's rows never arrived
     uint64_t shard_timeout_ns;
     unsigned long long *claim;    // [n_slots] epoch of the last claim
@@ -227,20 +227,21 @@ template <> __device__ __forceinline__ void store_out<L2D_BF16>(uint8_t *y, floa
 }
 
 // Shared-memory staging of the x vectors of problems [b0, b0 + nb): returns the base pointer the
-// row code indexes as xs + (b - b0) * row_bytes.
+// row code indexes as xs + (b - b0) * row_bytes.  cp.async puts every 16-byte chunk of a thread in
+// flight at once without holding registers, so staging costs about one round trip to L2.
 __device__ __forceinline__ const uint8_t *stage_x(const GemvArgs &a, uint8_t *smem, int64_t b0, int64_t nb) {
     const int64_t rb16 = (a.row_bytes + 15) & ~int64_t(15);
+    const int64_t full16 = a.row_bytes / 16;
     for (int64_t b = 0; b < nb; ++b) {
         const uint8_t *src = a.x + (b0 + b) * a.stride_x_bytes;
         uint8_t *dst = smem + b * rb16;
-        for (int64_t o = threadIdx.x * 16; o < rb16; o += blockDim.x * 16) {
-            if (o + 16 <= a.row_bytes) {
-                *reinterpret_cast<uint4 *>(dst + o) = *reinterpret_cast<const uint4 *>(src + o);
-            } else {
-                for (int64_t k = o; k < o + 16; ++k) dst[k] = k < a.row_bytes ? src[k] : 0;
-            }
+        for (int64_t k = threadIdx.x; k < full16; k += blockDim.x) {
+            const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + 16 * k));
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src + 16 * k) : "memory");
         }
+        for (int64_t k = full16 * 16 + threadIdx.x; k < rb16; k += blockDim.x) dst[k] = k < a.row_bytes ? src[k] : 0;
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     return smem;
 }
@@ -280,17 +281,13 @@ __device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsig
     asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// Rows this CTA finished in this launch (sharded kernels count them for the peers' arrival counters).
-__shared__ unsigned int s_fin_rows;
-
 // Sharded, unsplit kernel, lane 0 after storing the final y of a row at yp: the same value into
-// every peer's gathered y (plain stores over NVLink, posted), and one more finished row.
+// every peer's gathered y (plain stores over NVLink, posted).
 template <int DT_OUT, bool SH> __device__ __forceinline__ void final_to_peers(const GemvArgs &a, uint8_t *yp, float v) {
     if (!SH) return;
     const int64_t off = a.y_shard_off + (yp - a.y);
     for (int p = 0; p < a.shard_world; ++p)
         if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + off, v);
-    atomicAdd_block(&s_fin_rows, 1u);
 }
 
 // One row of A for one domain group.  SPLITK: the split kernel (both groups visit every row and
@@ -418,7 +415,6 @@ __device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int
                         for (int p = 0; p < a.shard_world; ++p)
                             if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
                 }
-                if (SH) atomicAdd_block(&s_fin_rows, static_cast<unsigned int>(hi - lo));
                 a.meet[id] = 0u;
             }
         }
@@ -427,22 +423,34 @@ __device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int
     const int n = min(s_n, kMaxIv);
     if (n == 0) return;
     __threadfence();  // the other group's partials, counted before its arrival
+    constexpr int kCombineUnroll = 2;  // a thread's partial loads in flight together
     for (int k = 0; k < n; ++k) {
         const int64_t lo = s_lo[k], hi = s_hi[k];
-        for (int64_t r = lo + threadIdx.x; r < hi; r += blockDim.x) {
-            const float v = __ldcg(a.part + r) + __ldcg(a.part + a.rows_total + r);
-            const int64_t yi = y_index(a, r);
-            store_out<DT_OUT>(a.y + yi * eo, v);
-            if (SH)
-                for (int p = 0; p < a.shard_world; ++p)
-                    if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
+        for (int64_t r0 = lo + threadIdx.x; r0 < hi; r0 += static_cast<int64_t>(blockDim.x) * kCombineUnroll) {
+            float p0[kCombineUnroll], p1[kCombineUnroll];
+#pragma unroll
+            for (int u = 0; u < kCombineUnroll; ++u) {
+                const int64_t r = r0 + static_cast<int64_t>(u) * blockDim.x;
+                if (r < hi) {
+                    p0[u] = __ldcg(a.part + r);
+                    p1[u] = __ldcg(a.part + a.rows_total + r);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kCombineUnroll; ++u) {
+                const int64_t r = r0 + static_cast<int64_t>(u) * blockDim.x;
+                if (r >= hi) continue;
+                const float v = p0[u] + p1[u];
+                const int64_t yi = y_index(a, r);
+                store_out<DT_OUT>(a.y + yi * eo, v);
+                if (SH)
+                    for (int p = 0; p < a.shard_world; ++p)
+                        if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
+            }
         }
-        if (threadIdx.x == 0) {
-            a.meet[s_id[k]] = 0u;
-            if (SH) atomicAdd_block(&s_fin_rows, static_cast<unsigned int>(hi - lo));
-        }
+        if (threadIdx.x == 0) a.meet[s_id[k]] = 0u;
     }
-    if (SH) __threadfence_system();  // the peer copies before the CTA's count at its end
+    if (SH) __threadfence_system();  // the peer copies before the CTA reports done
     __syncthreads();
 }
 
@@ -459,7 +467,9 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     if (r0 >= r1) return;
     const uint8_t *xs = nullptr;
     int64_t b0 = 0;
-    if (a.x_smem) {
+    if (SH) {
+        xs = smem;  // staged once by the prologue (sharded calls are batch 1)
+    } else if (a.x_smem) {
         b0 = r0 / a.M;
         xs = stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
     }
@@ -495,48 +505,58 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-// Sharded prologue, one warp per CTA.  Rank 0: CTA i < x_slices pushes slice i of x to every peer
-// and counts it there.  Other ranks: wait (bounded) until all slices of this step have arrived.
-template <bool SH> __device__ __forceinline__ void shard_prologue(const GemvArgs &a, int lane) {
+// Sharded prologue, the whole CTA (batch 1, x staged once for all of the CTA's slots).
+//  Rank 0: CTA b stores its share of x's 4-byte words into every peer's flagged-word buffer as
+//  (word, step) pairs, 8-byte stores that arrive whole, then stages its own x.
+//  Other ranks: read their flagged-word buffer 16 bytes (two words) at a time until both flags
+//  carry this step (bounded by the timeout; status bit 0 when it runs out) and stage the words.
+template <bool SH> __device__ __forceinline__ void shard_stage_x(const GemvArgs &a, uint8_t *smem) {
     if (!SH) return;
+    const int64_t words = (a.x_bytes + 3) / 4;
+    const uint32_t flag = static_cast<uint32_t>(a.shard_epoch);
     if (a.shard_rank == 0) {
-        if (static_cast<int>(blockIdx.x) >= a.x_slices) return;
-        const int64_t n16 = a.x_bytes / 16;
-        const int64_t lo = n16 * blockIdx.x / a.x_slices, hi = n16 * (blockIdx.x + 1) / a.x_slices;
-        const bool tail = static_cast<int>(blockIdx.x) == a.x_slices - 1;
-        for (int p = 1; p < a.shard_world; ++p) {
-            for (int64_t k = lo + lane; k < hi; k += 32)
-                reinterpret_cast<uint4 *>(a.peer_x[p])[k] = reinterpret_cast<const uint4 *>(a.x)[k];
-            if (tail)
-                for (int64_t k = n16 * 16 + lane; k < a.x_bytes; k += 32) a.peer_x[p][k] = a.x[k];
+        const int64_t lo = words * blockIdx.x / gridDim.x, hi = words * (blockIdx.x + 1) / gridDim.x;
+        const uint32_t *xw = reinterpret_cast<const uint32_t *>(a.x);
+        for (int64_t w = lo + threadIdx.x; w < hi; w += blockDim.x) {
+            const uint32_t v = xw[w];
+            for (int p = 1; p < a.shard_world; ++p)
+                asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(a.peer_xw[p] + w), "r"(v), "r"(flag)
+                             : "memory");
         }
-        __threadfence_system();
-        __syncwarp();
-        if (lane >= 1 && lane < a.shard_world) red_release_sys_add(a.peer_arrive[lane], 1ull);
+        stage_x(a, smem, 0, 1);
         return;
     }
-    if (lane == 0) {
-        const unsigned long long want = a.shard_epoch * static_cast<unsigned long long>(a.x_slices);
-        const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
-        while (ld_acquire_sys(a.arrive) < want) {
+    const uint2 *xw = a.peer_xw[a.shard_rank];
+    uint32_t *dst = reinterpret_cast<uint32_t *>(smem);
+    const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
+    for (int64_t j = threadIdx.x; 2 * j < words; j += blockDim.x) {
+        const bool two = 2 * j + 1 < words;
+        uint32_t d0, f0, d1, f1;
+        for (;;) {
+            asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(d0), "=r"(f0), "=r"(d1), "=r"(f1)
+                         : "l"(xw + 2 * j)
+                         : "memory");
+            if (f0 == flag && (!two || f1 == flag)) break;
             if (dev::globaltimer_ns() > deadline) {
                 atomicOr(a.shard_status, 1u);
                 break;
             }
-            __nanosleep(100);
+            __nanosleep(64);
         }
+        dst[2 * j] = d0;
+        if (two) dst[2 * j + 1] = d1;
     }
-    __syncwarp();
+    __syncthreads();
 }
 
-// Sharded, every CTA at its end (after a barrier that follows every warp's system-scope fence):
-// this CTA's finished rows are added to every peer's arrival counter for this rank.
+// Sharded, the last CTA once every CTA has reported done: every CTA fenced its peer copies at
+// system scope before its done count, so one release per peer covers all of this rank's rows.
 template <bool SH> __device__ __forceinline__ void shard_signal(const GemvArgs &a) {
     if (!SH) return;
     const int p = threadIdx.x;
-    const unsigned int n = s_fin_rows;
-    if (p < a.shard_world && p != a.shard_rank && n != 0u)
-        red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, static_cast<unsigned long long>(n));
+    if (p < a.shard_world && p != a.shard_rank && a.rows_total > 0)
+        red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, static_cast<unsigned long long>(a.rows_total));
 }
 
 // Sharded epilogue (last CTA): wait (bounded) until every peer's rows of this step have arrived.
@@ -605,11 +625,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
             s_slot = got;
             s_epoch = E;
             s_count = 0;
-            if (SH) s_fin_rows = 0u;
         }
-        shard_prologue<SH>(a, lane);
     }
     __syncthreads();
+    shard_stage_x<SH>(a, smem);
     if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
     __syncthreads();
     if (tid == 0) {
@@ -619,10 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         if (s_last) __threadfence();  // acquire side: the other CTAs' y rows before the epilogue
     }
     __syncthreads();
-    if (!s_last) {
-        shard_signal<SH>(a);
-        return;
-    }
+    if (!s_last) return;
     // Last CTA: slots whose SM never hosted a CTA of this launch, found by one parallel sweep.
     const unsigned long long E = s_epoch;
     for (int t = tid; t < a.n_slots; t += blockDim.x) {
@@ -1079,8 +1095,8 @@ int check_args(const GemvArgs &a) {
     if (!a.x || !a.y || !a.sm_slot || !a.part || !a.meet || !a.claim || !a.ctl || a.n_slots <= 0 ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
-    if (a.shard_world > 1 && (!a.arrive || !a.peer_arrive || !a.peer_x || !a.peer_y || !a.rows_of ||
-                              !a.shard_status || a.x_slices <= 0))
+    if (a.shard_world > 1 && (!a.arrive || !a.peer_arrive || !a.peer_xw || !a.peer_y || !a.rows_of ||
+                              !a.shard_status || !a.x_smem || a.rows_total != a.M))
         return set_error(L2D_ERR_INVALID, "sharded gemv arguments incomplete (internal error)");
     return L2D_OK;
 }
@@ -1112,16 +1128,16 @@ int shard_fill_args(GemvArgs *a, const ShardArgs &sh) {
     a->shard_epoch = sh.epoch;
     a->arrive = sh.arrive;
     a->peer_arrive = sh.peer_arrive;
-    a->peer_x = sh.peer_x;
+    a->peer_xw = sh.peer_xw;
     a->peer_y = sh.peer_y;
     a->rows_of = sh.rows_of;
     a->y_shard_off = sh.y_shard_off;
     a->x_bytes = sh.x_bytes;
-    a->x_slices = sh.x_slices;
     a->shard_status = sh.status;
     a->shard_timeout_ns = sh.timeout_ns;
-    if (sh.world > 1 && a->n_slots < sh.x_slices)
-        return set_error(L2D_ERR_UNSUPPORTED, "sharded gemv needs >= %d CTAs, plan has %d", sh.x_slices, a->n_slots);
+    if (sh.world > 1 && !a->x_smem)
+        return set_error(L2D_ERR_UNSUPPORTED, "sharded gemv stages x in shared memory: N * element size <= %d bytes",
+                         kXSmemMax);
     return L2D_OK;
 }
 

@@ -3,6 +3,8 @@
 
 #include "l2d.h"
 
+#include <vector_types.h>
+
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -40,11 +42,10 @@ struct ShardArgs {
     unsigned long long epoch;
     unsigned long long *arrive;
     unsigned long long *const *peer_arrive;
-    uint8_t *const *peer_x;
+    uint2 *const *peer_xw;
     uint8_t *const *peer_y;
     const unsigned long long *rows_of;
     int64_t y_shard_off, x_bytes;
-    int x_slices;
     uint32_t *status;
     uint64_t timeout_ns;
 };

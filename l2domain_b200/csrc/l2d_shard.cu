@@ -4,13 +4,13 @@
 // gathers the y shards on every rank; instead of a broadcast and an all-gather launched around the
 // GEMV, every rank maps the other ranks' shard buffers (cudaIpcOpenMemHandle) and one GEMV launch
 // per rank and step does the exchange while it computes:
-//   * rank 0's first kXSlices CTAs each push one slice of x into every peer's x buffer and count it
-//     in that peer's x arrival counter (system-scope release); the other ranks' CTAs wait for all
-//     slices before they stage x;
-//   * whoever stores a row's final y (the domain group that finishes the row) also stores it into
-//     every peer's gathered y, so the gather runs under the GEMV as rows finish; each CTA counts
-//     the rows it finished and, after a system-scope fence, adds the count to every peer's arrival
-//     counter for this rank;
+//   * rank 0's CTAs each store a share of x into every peer's flagged-word buffer, as 8-byte
+//     (4 bytes of x, step number) pairs that arrive whole; the other ranks' CTAs read the pairs
+//     until every flag carries the step while they stage x, so x needs no fence and no counter;
+//   * the CTA that finishes an interval of rows (the second of the two domain-group slots that
+//     cover it) stores the final y into its own gathered y and into every peer's, so the gather
+//     runs under the GEMV; every CTA fences those stores at system scope before it reports done,
+//     and the last CTA adds the rank's row count to every peer's arrival counter for this rank;
 //   * the last CTA waits until every peer's rows of the step have arrived.
 // x and y are double-buffered by the parity of the step number, so a step never overwrites data a
 // peer may still read from the step before (a rank enters step e+1 only after every peer's step-e
@@ -43,15 +43,15 @@ size_t gemv_args_size();
 namespace shard {
 
 constexpr uint32_t kMagic = 0x4c32445du;  // "L2D]"
-constexpr uint32_t kVersion = 2;
+constexpr uint32_t kVersion = 3;
 constexpr int kMaxWorld = 64;
-constexpr int kXSlices = 32;    // x is pushed in this many slices, one per CTA of rank 0
+constexpr int kIdleCtas = 32;   // grid of the step of a rank without rows
 
 struct Blob {
     uint32_t magic, version;
     int32_t pid, rank, world, device;
     int64_t bytes, rows;
-    int32_t x_slices, reserved;
+    int32_t reserved0, reserved1;
     uint64_t raw;  // device address in the exporting process (used when importer == exporter)
     cudaIpcMemHandle_t handle;
 };
@@ -62,27 +62,20 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
     return v;
 }
 
-__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// The step of a rank without rows (M_total < world): rank 0 still pushes x (kXSlices CTAs of one
-// warp, as the GEMV prologue does), and CTA 0 waits for the peers' rows.
+// The step of a rank without rows (M_total < world): rank 0 still pushes x as flagged words (as
+// the GEMV prologue does), and CTA 0 waits for the peers' rows.
 __global__ void k_shard_idle(ShardArgs sh, const uint8_t *x) {
     const int lane = threadIdx.x;
     if (sh.rank == 0 && sh.world > 1) {
-        const int64_t n16 = sh.x_bytes / 16;
-        const int64_t lo = n16 * blockIdx.x / sh.x_slices, hi = n16 * (blockIdx.x + 1) / sh.x_slices;
-        const bool tail = static_cast<int>(blockIdx.x) == sh.x_slices - 1;
-        for (int p = 1; p < sh.world; ++p) {
-            for (int64_t k = lo + lane; k < hi; k += 32)
-                reinterpret_cast<uint4 *>(sh.peer_x[p])[k] = reinterpret_cast<const uint4 *>(x)[k];
-            if (tail)
-                for (int64_t k = n16 * 16 + lane; k < sh.x_bytes; k += 32) sh.peer_x[p][k] = x[k];
+        const int64_t words = (sh.x_bytes + 3) / 4;
+        const int64_t lo = words * blockIdx.x / gridDim.x, hi = words * (blockIdx.x + 1) / gridDim.x;
+        const uint32_t flag = static_cast<uint32_t>(sh.epoch);
+        for (int64_t w = lo + lane; w < hi; w += blockDim.x) {
+            const uint32_t v = reinterpret_cast<const uint32_t *>(x)[w];
+            for (int p = 1; p < sh.world; ++p)
+                asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(sh.peer_xw[p] + w), "r"(v), "r"(flag)
+                             : "memory");
         }
-        __threadfence_system();
-        __syncwarp();
-        if (lane >= 1 && lane < sh.world) red_release_sys_add(sh.peer_arrive[lane], 1ull);
     }
     if (blockIdx.x != 0) return;
     for (int p = lane; p < sh.world; p += 32) {
@@ -111,10 +104,10 @@ struct l2d_shard {
     uint64_t timeout_ns = 0;
     uint8_t *base = nullptr;  // shared allocation: arrival counters, x[2], y[2]
     size_t bytes = 0;
-    size_t off_arrive = 0, off_x[2] = {0, 0}, off_y[2] = {0, 0};
+    size_t off_arrive = 0, off_x[2] = {0, 0}, off_xw[2] = {0, 0}, off_y[2] = {0, 0};
     std::vector<uint8_t *> peer;  // [world] peer bases in this process's address space
     std::vector<bool> opened;     // opened through IPC (closed on destroy)
-    // Local device tables: peer_x[2][world], peer_y[2][world], peer_arrive[world] (pointers),
+    // Local device tables: peer_xw[2][world], peer_y[2][world], peer_arrive[world] (pointers),
     // rows_of[world] (u64), status (u32).
     uint8_t *tables = nullptr;
     size_t off_rows_of = 0, off_status = 0, tables_bytes = 0;
@@ -126,7 +119,7 @@ using namespace l2d;
 
 namespace {
 
-uint8_t **tab_x(l2d_shard *s, int par) { return reinterpret_cast<uint8_t **>(s->tables) + par * s->world; }
+uint2 **tab_xw(l2d_shard *s, int par) { return reinterpret_cast<uint2 **>(s->tables) + par * s->world; }
 uint8_t **tab_y(l2d_shard *s, int par) { return reinterpret_cast<uint8_t **>(s->tables) + (2 + par) * s->world; }
 unsigned long long **tab_arrive(l2d_shard *s) {
     return reinterpret_cast<unsigned long long **>(s->tables) + 4 * s->world;
@@ -155,12 +148,11 @@ ShardArgs shard_args(l2d_shard *s, int par, unsigned long long e) {
     sh.epoch = e;
     sh.arrive = reinterpret_cast<unsigned long long *>(s->base + s->off_arrive);
     sh.peer_arrive = tab_arrive(s);
-    sh.peer_x = tab_x(s, par);
+    sh.peer_xw = tab_xw(s, par);
     sh.peer_y = tab_y(s, par);
     sh.rows_of = tab_rows_of(s);
     sh.y_shard_off = s->row0 * s->eb_out;
     sh.x_bytes = s->N * s->eb_in;
-    sh.x_slices = shard::kXSlices;
     sh.status = status_word(s);
     sh.timeout_ns = s->timeout_ns;
     return sh;
@@ -205,6 +197,11 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
         s->off_x[par] = off;
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(N, 1)) * s->eb_in);
     }
+    const size_t words = (static_cast<size_t>(std::max<int64_t>(N, 1)) * s->eb_in + 3) / 4;
+    for (int par = 0; par < 2; ++par) {
+        s->off_xw[par] = off;
+        off += shard::up256(words * sizeof(uint2));
+    }
     for (int par = 0; par < 2; ++par) {
         s->off_y[par] = off;
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(M_total, 1)) * s->eb_out);
@@ -248,7 +245,6 @@ int l2d_shard_handle(const l2d_shard *s, void *blob, size_t cap, size_t *len) {
     b.device = s->device;
     b.bytes = static_cast<int64_t>(s->bytes);
     b.rows = s->rows;
-    b.x_slices = shard::kXSlices;
     b.raw = reinterpret_cast<uint64_t>(s->base);
     L2D_CUDA_TRY(cudaIpcGetMemHandle(&b.handle, s->base));
     std::memcpy(blob, &b, sizeof b);
@@ -268,7 +264,7 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
         shard::Blob b;
         std::memcpy(&b, static_cast<const uint8_t *>(blobs) + r * blob_len, sizeof b);
         if (b.magic != shard::kMagic || b.version != shard::kVersion || b.rank != r || b.world != s->world ||
-            b.bytes != static_cast<int64_t>(s->bytes) || b.x_slices != shard::kXSlices || b.rows < 0)
+            b.bytes != static_cast<int64_t>(s->bytes) || b.rows < 0)
             return set_error(L2D_ERR_INVALID, "shard blob %d does not match this shard layout", r);
         rows_of[r] = static_cast<unsigned long long>(b.rows);
         rows_sum += b.rows;
@@ -290,7 +286,7 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
     std::vector<uint8_t *> host(5 * s->world);
     for (int par = 0; par < 2; ++par)
         for (int r = 0; r < s->world; ++r) {
-            host[par * s->world + r] = s->peer[r] + s->off_x[par];
+            host[par * s->world + r] = s->peer[r] + s->off_xw[par];
             host[(2 + par) * s->world + r] = s->peer[r] + s->off_y[par];
         }
     for (int r = 0; r < s->world; ++r) host[4 * s->world + r] = s->peer[r] + s->off_arrive;
@@ -337,7 +333,7 @@ int l2d_gemv_sharded(l2d_plan *plan, l2d_shard *s, int mode, void *stream, int *
         if (st == L2D_OK) st = launch_args(plan, *a, split, stream);
         if (st != L2D_OK) return st;
     } else if (s->world > 1) {
-        shard::k_shard_idle<<<shard::kXSlices, 32, 0, cs>>>(sh, s->base + s->off_x[par]);
+        shard::k_shard_idle<<<shard::kIdleCtas, 32, 0, cs>>>(sh, s->base + s->off_x[par]);
         L2D_CUDA_TRY(cudaGetLastError());
     }
     s->epoch = e;  // only a launched step advances the step number (all ranks must stay in step)
