@@ -230,10 +230,13 @@ L2D_API int l2d_gemv_noalloc(const l2d_gemv_desc *desc, const l2d_domain_map *ma
  *      rank 0 writes x into l2d_shard_buffers(l2d_shard_next_parity()) .x, then every rank calls
  *      l2d_gemv_sharded; after it (stream-ordered) the gathered y of all M_total rows is in that
  *      parity's .y buffer on every rank.  Consume it on the same stream before the next step.
- * Rank 0 pushes x to the peers over NVLink; each rank's GEMV waits for it, then pushes its y rows to
- * every peer; a last kernel waits for all peers' rows.  Every wait is bounded by timeout_ms (0 =
- * 2000 ms); a timeout sets a bit in l2d_shard_status (1: x never arrived, 2: a peer's rows never
- * arrived) and the kernels return, leaving the context usable.  Peer memory sees plain loads/stores. */
+ * One kernel per rank and step: rank 0's CTAs store x into every peer's memory over NVLink, each
+ * final y row is stored into every peer's memory as it is finished, and every CTA collects its share
+ * of the other ranks' rows at its end; each transfer is a flagged 8-byte word the reader retries
+ * until it carries the step, so no fence or counter is involved.  Every retry is bounded by
+ * timeout_ms (0 = 2000 ms); a timeout sets a bit in l2d_shard_status (1: x never arrived, 2: a
+ * peer's rows never arrived) and the kernel returns, leaving the context usable.  Peers only store
+ * into each other's memory; nothing loads from a peer. */
 typedef struct l2d_shard l2d_shard;
 L2D_API int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t row0, int64_t rows,
                              int64_t N, int dtype_in, int dtype_out, uint32_t timeout_ms, l2d_shard **shard);

@@ -72,21 +72,19 @@ struct GemvArgs {
     int big_grp;                  // the group with more SMs
     float *part;                  // [2][rows_total] each domain group's partial of each row (split calls)
     unsigned int *meet;           // [n_slots] arrivals per interval of the two groups' slot partitions, zero between calls
-    // Peer-memory row sharding (shard_world > 1; batch 1).  Rank 0's CTAs push x to every peer as
-    // flagged 8-byte words (4 bytes of x, the step number), which the other ranks' CTAs check while
-    // they stage x: no fence and no counter on the way in.  Whoever stores a row's final y also
-    // stores it into every peer's gathered y and fences at system scope before its CTA reports
-    // done; the last CTA adds the rank's rows to every peer's arrival counter for this rank, then
-    // waits until every peer's rows of this step have arrived.
+    // Peer-memory row sharding (shard_world > 1; batch 1).  Every exchange is a flagged 8-byte
+    // word (4 bytes of data, the step number) stored into a peer's buffer; a reader retries a word
+    // until its flag carries the step, so nothing on the way needs a fence or a counter.  Rank 0's
+    // CTAs push x, the other ranks check the words while they stage x.  Whoever stores a row's
+    // final y also stores it into every peer's flagged y words; at its end every CTA takes its
+    // share of the other ranks' rows from its own flagged words into the gathered y.
     int shard_world;
     int shard_rank;
-    unsigned long long shard_epoch;     // step number (1, 2, ...): arrival targets are multiples of it
-    unsigned long long *arrive;         // this rank's arrival counters: [1 + r] rows of rank r
-    unsigned long long *const *peer_arrive;  // [world] each rank's arrival counters
-    uint2 *const *peer_xw;              // [world] each rank's flagged-word x buffer of this step's parity
-    uint8_t *const *peer_y;             // [world] each rank's gathered y buffer of this step's parity
-    const unsigned long long *rows_of;  // [world] rows of each rank
-    int64_t y_shard_off;                // byte offset of this rank's rows in the gathered y
+    unsigned long long shard_epoch;     // step number (1, 2, ...): the flag of this step's words
+    uint2 *const *peer_xw;              // [world] each rank's flagged x words of this step's parity
+    uint2 *const *peer_yw;              // [world] each rank's flagged y words (one per gathered row)
+    int64_t row0;                       // this rank's first row in the gathered y
+    int64_t rows_all;                   // rows of the gathered y (all ranks)
     int64_t x_bytes;
     uint32_t *shard_status;             // bit 0: x never arrived, bit 1: a peer's rows never arrived
     uint64_t shard_timeout_ns;
@@ -277,17 +275,25 @@ struct RowIter {  // rows_total < 2^31 (checked when the call is set up)
     }
 };
 
-__device__ __forceinline__ void red_release_sys_add(unsigned long long *p, unsigned long long v) {
-    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+template <int DT> __device__ __forceinline__ uint32_t out_bits(float v);
+template <> __device__ __forceinline__ uint32_t out_bits<L2D_F32>(float v) { return __float_as_uint(v); }
+template <> __device__ __forceinline__ uint32_t out_bits<L2D_F16>(float v) {
+    return __half_as_ushort(__float2half_rn(v));
+}
+template <> __device__ __forceinline__ uint32_t out_bits<L2D_BF16>(float v) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
-// Sharded, unsplit kernel, lane 0 after storing the final y of a row at yp: the same value into
-// every peer's gathered y (plain stores over NVLink, posted).
-template <int DT_OUT, bool SH> __device__ __forceinline__ void final_to_peers(const GemvArgs &a, uint8_t *yp, float v) {
+// Sharded: the final y of this rank's row r (batch 1) into every peer's flagged y words, as one
+// 8-byte store per peer (posted over NVLink; the word arrives whole).
+template <int DT_OUT, bool SH> __device__ __forceinline__ void final_to_peers(const GemvArgs &a, int64_t r, float v) {
     if (!SH) return;
-    const int64_t off = a.y_shard_off + (yp - a.y);
+    const uint32_t bits = out_bits<DT_OUT>(v), flag = static_cast<uint32_t>(a.shard_epoch);
     for (int p = 0; p < a.shard_world; ++p)
-        if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + off, v);
+        if (p != a.shard_rank)
+            asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(a.peer_yw[p] + a.row0 + r), "r"(bits),
+                         "r"(flag)
+                         : "memory");
 }
 
 // One row of A for one domain group.  SPLITK: the split kernel (both groups visit every row and
@@ -365,7 +371,7 @@ __device__ __forceinline__ void gemv_row(const GemvArgs &a, const RowIter &it, b
     } else {
         uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
         store_out<DT_OUT>(yp, sum);
-        final_to_peers<DT_OUT, SH>(a, yp, sum);
+        final_to_peers<DT_OUT, SH>(a, row, sum);
     }
 }
 
@@ -409,11 +415,8 @@ __device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int
                 __threadfence();
                 for (int64_t r = lo; r < hi; ++r) {
                     const float v = __ldcg(a.part + r) + __ldcg(a.part + a.rows_total + r);
-                    const int64_t yi = y_index(a, r);
-                    store_out<DT_OUT>(a.y + yi * eo, v);
-                    if (SH)
-                        for (int p = 0; p < a.shard_world; ++p)
-                            if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
+                    store_out<DT_OUT>(a.y + y_index(a, r) * eo, v);
+                    final_to_peers<DT_OUT, SH>(a, r, v);
                 }
                 a.meet[id] = 0u;
             }
@@ -441,16 +444,12 @@ __device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int
                 const int64_t r = r0 + static_cast<int64_t>(u) * blockDim.x;
                 if (r >= hi) continue;
                 const float v = p0[u] + p1[u];
-                const int64_t yi = y_index(a, r);
-                store_out<DT_OUT>(a.y + yi * eo, v);
-                if (SH)
-                    for (int p = 0; p < a.shard_world; ++p)
-                        if (p != a.shard_rank) store_out<DT_OUT>(a.peer_y[p] + a.y_shard_off + yi * eo, v);
+                store_out<DT_OUT>(a.y + y_index(a, r) * eo, v);
+                final_to_peers<DT_OUT, SH>(a, r, v);
             }
         }
         if (threadIdx.x == 0) a.meet[s_id[k]] = 0u;
     }
-    if (SH) __threadfence_system();  // the peer copies before the CTA reports done
     __syncthreads();
 }
 
@@ -484,25 +483,13 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
         if (spill && small_grp) continue;
         gemv_row<DT_IN, DT_OUT, SPLIT, SH>(a, it, SPLIT && !spill, grp, lane, xs, b0);
     }
-    if (lane == 0) {
-        if (SH && !SPLIT) {
-            __threadfence_system();  // the peer copies of this warp's rows before the CTA's count
-        } else {
-            __threadfence();  // this warp's partials (or y) before the slot's arrival / the CTA's done count
-        }
-    }
+    if (lane == 0) __threadfence();  // this warp's partials (or y) before the slot's arrival / the CTA's done count
     if (SPLIT) {
         __syncthreads();
         meet_and_combine<DT_OUT, SH>(a, grp, idx, r0, r1);
     } else if (a.x_smem) {
         __syncthreads();  // the staged x may be replaced for the next slot
     }
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
 }
 
 // Sharded prologue, the whole CTA (batch 1, x staged once for all of the CTA's slots).
@@ -550,31 +537,49 @@ template <bool SH> __device__ __forceinline__ void shard_stage_x(const GemvArgs 
     __syncthreads();
 }
 
-// Sharded, the last CTA once every CTA has reported done: every CTA fenced its peer copies at
-// system scope before its done count, so one release per peer covers all of this rank's rows.
-template <bool SH> __device__ __forceinline__ void shard_signal(const GemvArgs &a) {
+// Sharded, every CTA at its end: its share of the other ranks' rows (gathered rows outside
+// [row0, row0 + rows_total)), read from this rank's flagged y words 16 bytes (two rows) at a time
+// until both flags carry this step (bounded by the timeout; status bit 1 when it runs out), into the
+// gathered y.
+template <int DT_OUT, bool SH> __device__ __forceinline__ void shard_gather(const GemvArgs &a) {
     if (!SH) return;
-    const int p = threadIdx.x;
-    if (p < a.shard_world && p != a.shard_rank && a.rows_total > 0)
-        red_release_sys_add(a.peer_arrive[p] + 1 + a.shard_rank, static_cast<unsigned long long>(a.rows_total));
-}
-
-// Sharded epilogue (last CTA): wait (bounded) until every peer's rows of this step have arrived.
-template <bool SH> __device__ __forceinline__ void shard_final_wait(const GemvArgs &a) {
-    if (!SH) return;
-    const int p = threadIdx.x;
-    if (p < a.shard_world && p != a.shard_rank) {
-        const unsigned long long want = a.shard_epoch * a.rows_of[p];
-        const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
-        while (ld_acquire_sys(a.arrive + 1 + p) < want) {
+    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    const int64_t foreign = a.rows_all - a.rows_total;
+    if (foreign <= 0) return;
+    // Pairs of gathered rows (2k, 2k+1) whose first row is foreign, split over the CTAs.
+    const int64_t pairs = (a.rows_all + 1) / 2;
+    const int64_t lo = pairs * blockIdx.x / gridDim.x, hi = pairs * (blockIdx.x + 1) / gridDim.x;
+    const uint2 *yw = a.peer_yw[a.shard_rank];
+    uint8_t *y_all = a.y - a.row0 * eo;
+    const uint32_t flag = static_cast<uint32_t>(a.shard_epoch);
+    const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
+    const int64_t own_lo = a.row0, own_hi = a.row0 + a.rows_total;
+    for (int64_t k = lo + threadIdx.x; k < hi; k += blockDim.x) {
+        const int64_t g = 2 * k;
+        const bool f0 = g < own_lo || g >= own_hi;
+        const bool f1 = g + 1 < a.rows_all && (g + 1 < own_lo || g + 1 >= own_hi);
+        if (!f0 && !f1) continue;
+        uint32_t d0, l0, d1, l1;
+        for (;;) {
+            asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(d0), "=r"(l0), "=r"(d1), "=r"(l1)
+                         : "l"(yw + g)
+                         : "memory");
+            if ((!f0 || l0 == flag) && (!f1 || l1 == flag)) break;
             if (dev::globaltimer_ns() > deadline) {
                 atomicOr(a.shard_status, 2u);
                 break;
             }
-            __nanosleep(100);
+            __nanosleep(64);
+        }
+        if (eo == 4) {
+            if (f0) reinterpret_cast<uint32_t *>(y_all)[g] = d0;
+            if (f1) reinterpret_cast<uint32_t *>(y_all)[g + 1] = d1;
+        } else {
+            if (f0) reinterpret_cast<uint16_t *>(y_all)[g] = static_cast<uint16_t>(d0);
+            if (f1) reinterpret_cast<uint16_t *>(y_all)[g + 1] = static_cast<uint16_t>(d1);
         }
     }
-    __syncthreads();
 }
 
 __device__ __forceinline__ unsigned long long ld_claim(const unsigned long long *p) {
@@ -638,7 +643,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         if (s_last) __threadfence();  // acquire side: the other CTAs' y rows before the epilogue
     }
     __syncthreads();
-    if (!s_last) return;
+    if (!s_last) {
+        shard_gather<DT_OUT, SH>(a);
+        return;
+    }
     // Last CTA: slots whose SM never hosted a CTA of this launch, found by one parallel sweep.
     const unsigned long long E = s_epoch;
     for (int t = tid; t < a.n_slots; t += blockDim.x) {
@@ -651,8 +659,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
         __syncthreads();
     }
-    shard_signal<SH>(a);
-    shard_final_wait<SH>(a);
+    shard_gather<DT_OUT, SH>(a);
     if (tid == 0) {
         a.ctl[1] = 0ull;
         __threadfence();
@@ -1095,8 +1102,8 @@ int check_args(const GemvArgs &a) {
     if (!a.x || !a.y || !a.sm_slot || !a.part || !a.meet || !a.claim || !a.ctl || a.n_slots <= 0 ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
-    if (a.shard_world > 1 && (!a.arrive || !a.peer_arrive || !a.peer_xw || !a.peer_y || !a.rows_of ||
-                              !a.shard_status || !a.x_smem || a.rows_total != a.M))
+    if (a.shard_world > 1 && (!a.peer_xw || !a.peer_yw || !a.shard_status || !a.x_smem || a.rows_total != a.M ||
+                              a.row0 < 0 || a.row0 + a.rows_total > a.rows_all))
         return set_error(L2D_ERR_INVALID, "sharded gemv arguments incomplete (internal error)");
     return L2D_OK;
 }
@@ -1126,12 +1133,10 @@ int shard_fill_args(GemvArgs *a, const ShardArgs &sh) {
     a->shard_world = sh.world;
     a->shard_rank = sh.rank;
     a->shard_epoch = sh.epoch;
-    a->arrive = sh.arrive;
-    a->peer_arrive = sh.peer_arrive;
     a->peer_xw = sh.peer_xw;
-    a->peer_y = sh.peer_y;
-    a->rows_of = sh.rows_of;
-    a->y_shard_off = sh.y_shard_off;
+    a->peer_yw = sh.peer_yw;
+    a->row0 = sh.row0;
+    a->rows_all = sh.rows_all;
     a->x_bytes = sh.x_bytes;
     a->shard_status = sh.status;
     a->shard_timeout_ns = sh.timeout_ns;

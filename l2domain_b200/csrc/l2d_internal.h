@@ -40,12 +40,9 @@ int cached_sm_map(int device, std::vector<int> &out);
 struct ShardArgs {
     int world, rank;
     unsigned long long epoch;
-    unsigned long long *arrive;
-    unsigned long long *const *peer_arrive;
     uint2 *const *peer_xw;
-    uint8_t *const *peer_y;
-    const unsigned long long *rows_of;
-    int64_t y_shard_off, x_bytes;
+    uint2 *const *peer_yw;
+    int64_t row0, rows_all, x_bytes;
     uint32_t *status;
     uint64_t timeout_ns;
 };

@@ -2,22 +2,22 @@
 //
 // The reference has no multi-GPU path.  The row-sharded configuration broadcasts x from rank 0 and
 // gathers the y shards on every rank; instead of a broadcast and an all-gather launched around the
-// GEMV, every rank maps the other ranks' shard buffers (cudaIpcOpenMemHandle) and one GEMV launch
-// per rank and step does the exchange while it computes:
-//   * rank 0's CTAs each store a share of x into every peer's flagged-word buffer, as 8-byte
-//     (4 bytes of x, step number) pairs that arrive whole; the other ranks' CTAs read the pairs
-//     until every flag carries the step while they stage x, so x needs no fence and no counter;
+// GEMV, every rank maps the other ranks' exchange buffers (cudaIpcOpenMemHandle) and one GEMV
+// launch per rank and step does the exchange while it computes.  Every transfer is a flagged
+// 8-byte word -- 4 bytes of data and the step number -- written with one store into the reader's
+// memory; the reader retries a word until its flag carries the step, so no fence, counter or
+// barrier is on the way (the protocol NCCL calls LL):
+//   * rank 0's CTAs store x into every peer's x words; the other ranks check them while they stage
+//     x into shared memory;
 //   * the CTA that finishes an interval of rows (the second of the two domain-group slots that
-//     cover it) stores the final y into its own gathered y and into every peer's, so the gather
-//     runs under the GEMV; every CTA fences those stores at system scope before it reports done,
-//     and the last CTA adds the rank's row count to every peer's arrival counter for this rank;
-//   * the last CTA waits until every peer's rows of the step have arrived.
-// x and y are double-buffered by the parity of the step number, so a step never overwrites data a
-// peer may still read from the step before (a rank enters step e+1 only after every peer's step-e
-// rows arrived, i.e. after every peer finished reading step e-1's buffers).  Arrival counters only
-// grow: the target of step e is e times the per-step count.  Every wait is bounded by %globaltimer;
-// a timeout sets a status bit (l2d_shard_status) and the kernel returns.  No TMA or bulk-copy load
-// touches peer memory: only plain loads and stores.
+//     cover it) stores each final y into its own gathered y and into every peer's y words;
+//   * at its end every CTA takes its share of the other ranks' rows from its own y words into the
+//     gathered y.
+// The words are double-buffered by the parity of the step number: a rank writes step e+2's words
+// only after its step e+1, which needed the reader's step e+1 words, i.e. after the reader
+// finished step e.  Every retry loop is bounded by %globaltimer; a timeout sets a status bit
+// (l2d_shard_status) and the kernel returns.  No TMA or bulk-copy load touches peer memory: only
+// plain stores and the readers' loads of their own memory.
 #include "l2d_device.cuh"
 #include "l2d_internal.h"
 
@@ -56,15 +56,9 @@ struct Blob {
     cudaIpcMemHandle_t handle;
 };
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
 // The step of a rank without rows (M_total < world): rank 0 still pushes x as flagged words (as
-// the GEMV prologue does), and CTA 0 waits for the peers' rows.
-__global__ void k_shard_idle(ShardArgs sh, const uint8_t *x) {
+// the GEMV prologue does), and every row of the gathered y comes from the peers' words.
+__global__ void k_shard_idle(ShardArgs sh, const uint8_t *x, uint8_t *y_all, int eo) {
     const int lane = threadIdx.x;
     if (sh.rank == 0 && sh.world > 1) {
         const int64_t words = (sh.x_bytes + 3) / 4;
@@ -77,17 +71,25 @@ __global__ void k_shard_idle(ShardArgs sh, const uint8_t *x) {
                              : "memory");
         }
     }
-    if (blockIdx.x != 0) return;
-    for (int p = lane; p < sh.world; p += 32) {
-        if (p == sh.rank) continue;
-        const unsigned long long want = sh.epoch * sh.rows_of[p];
-        const uint64_t deadline = dev::globaltimer_ns() + sh.timeout_ns;
-        while (ld_acquire_sys(sh.arrive + 1 + p) < want) {
+    const uint32_t flag = static_cast<uint32_t>(sh.epoch);
+    const uint64_t deadline = dev::globaltimer_ns() + sh.timeout_ns;
+    const uint2 *yw = sh.peer_yw[sh.rank];
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + lane; g < sh.rows_all;
+         g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        uint32_t d, f;
+        for (;;) {
+            asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(d), "=r"(f) : "l"(yw + g) : "memory");
+            if (f == flag) break;
             if (dev::globaltimer_ns() > deadline) {
                 atomicOr(sh.status, 2u);
-                break;
+                return;
             }
-            __nanosleep(100);
+            __nanosleep(64);
+        }
+        if (eo == 4) {
+            reinterpret_cast<uint32_t *>(y_all)[g] = d;
+        } else {
+            reinterpret_cast<uint16_t *>(y_all)[g] = static_cast<uint16_t>(d);
         }
     }
 }
@@ -102,15 +104,14 @@ struct l2d_shard {
     int64_t M_total = 0, row0 = 0, rows = 0, N = 0;
     int dtype_in = 0, dtype_out = 0, eb_in = 4, eb_out = 4;
     uint64_t timeout_ns = 0;
-    uint8_t *base = nullptr;  // shared allocation: arrival counters, x[2], y[2]
+    uint8_t *base = nullptr;  // shared allocation: x[2], x words[2], y[2], y words[2]
     size_t bytes = 0;
-    size_t off_arrive = 0, off_x[2] = {0, 0}, off_xw[2] = {0, 0}, off_y[2] = {0, 0};
+    size_t off_x[2] = {0, 0}, off_xw[2] = {0, 0}, off_y[2] = {0, 0}, off_yw[2] = {0, 0};
     std::vector<uint8_t *> peer;  // [world] peer bases in this process's address space
     std::vector<bool> opened;     // opened through IPC (closed on destroy)
-    // Local device tables: peer_xw[2][world], peer_y[2][world], peer_arrive[world] (pointers),
-    // rows_of[world] (u64), status (u32).
+    // Local device tables: peer_xw[2][world], peer_yw[2][world] (pointers), status (u32).
     uint8_t *tables = nullptr;
-    size_t off_rows_of = 0, off_status = 0, tables_bytes = 0;
+    size_t off_status = 0, tables_bytes = 0;
     bool connected = false;
     unsigned long long epoch = 0;
 };
@@ -120,13 +121,7 @@ using namespace l2d;
 namespace {
 
 uint2 **tab_xw(l2d_shard *s, int par) { return reinterpret_cast<uint2 **>(s->tables) + par * s->world; }
-uint8_t **tab_y(l2d_shard *s, int par) { return reinterpret_cast<uint8_t **>(s->tables) + (2 + par) * s->world; }
-unsigned long long **tab_arrive(l2d_shard *s) {
-    return reinterpret_cast<unsigned long long **>(s->tables) + 4 * s->world;
-}
-unsigned long long *tab_rows_of(l2d_shard *s) {
-    return reinterpret_cast<unsigned long long *>(s->tables + s->off_rows_of);
-}
+uint2 **tab_yw(l2d_shard *s, int par) { return reinterpret_cast<uint2 **>(s->tables) + (2 + par) * s->world; }
 uint32_t *status_word(l2d_shard *s) { return reinterpret_cast<uint32_t *>(s->tables + s->off_status); }
 
 struct DeviceScope {
@@ -146,12 +141,10 @@ ShardArgs shard_args(l2d_shard *s, int par, unsigned long long e) {
     sh.world = s->world;
     sh.rank = s->rank;
     sh.epoch = e;
-    sh.arrive = reinterpret_cast<unsigned long long *>(s->base + s->off_arrive);
-    sh.peer_arrive = tab_arrive(s);
     sh.peer_xw = tab_xw(s, par);
-    sh.peer_y = tab_y(s, par);
-    sh.rows_of = tab_rows_of(s);
-    sh.y_shard_off = s->row0 * s->eb_out;
+    sh.peer_yw = tab_yw(s, par);
+    sh.row0 = s->row0;
+    sh.rows_all = s->M_total;
     sh.x_bytes = s->N * s->eb_in;
     sh.status = status_word(s);
     sh.timeout_ns = s->timeout_ns;
@@ -191,8 +184,6 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
     s->eb_out = elem_bytes(dtype_out);
     s->timeout_ns = static_cast<uint64_t>(timeout_ms ? timeout_ms : 2000u) * 1000000ull;
     size_t off = 0;
-    s->off_arrive = off;
-    off += shard::up256((1 + world) * sizeof(unsigned long long));
     for (int par = 0; par < 2; ++par) {
         s->off_x[par] = off;
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(N, 1)) * s->eb_in);
@@ -206,9 +197,12 @@ int l2d_shard_create(int device, int rank, int world, int64_t M_total, int64_t r
         s->off_y[par] = off;
         off += shard::up256(static_cast<size_t>(std::max<int64_t>(M_total, 1)) * s->eb_out);
     }
+    for (int par = 0; par < 2; ++par) {
+        s->off_yw[par] = off;
+        off += shard::up256(static_cast<size_t>(std::max<int64_t>(M_total, 1)) * sizeof(uint2));
+    }
     s->bytes = off;
-    s->off_rows_of = 5 * world * sizeof(void *);
-    s->off_status = s->off_rows_of + world * sizeof(unsigned long long);
+    s->off_status = 4 * world * sizeof(void *);
     s->tables_bytes = s->off_status + 16;
     cudaError_t e = cudaMalloc(&s->base, s->bytes);
     if (e == cudaSuccess) e = cudaMemset(s->base, 0, s->bytes);
@@ -258,7 +252,7 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
                          sizeof(shard::Blob));
     DeviceScope scope(s->device);
     const pid_t me = getpid();
-    std::vector<unsigned long long> rows_of(s->world, 0);
+
     int64_t rows_sum = 0;
     for (int r = 0; r < s->world; ++r) {
         shard::Blob b;
@@ -266,7 +260,6 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
         if (b.magic != shard::kMagic || b.version != shard::kVersion || b.rank != r || b.world != s->world ||
             b.bytes != static_cast<int64_t>(s->bytes) || b.rows < 0)
             return set_error(L2D_ERR_INVALID, "shard blob %d does not match this shard layout", r);
-        rows_of[r] = static_cast<unsigned long long>(b.rows);
         rows_sum += b.rows;
         if (r == s->rank || s->peer[r]) continue;
         if (b.pid == static_cast<int32_t>(me)) {
@@ -283,16 +276,13 @@ int l2d_shard_connect(l2d_shard *s, const void *blobs, size_t blob_len) {
     if (rows_sum != s->M_total)
         return set_error(L2D_ERR_INVALID, "the ranks' rows add up to %lld, not M_total = %lld",
                          static_cast<long long>(rows_sum), static_cast<long long>(s->M_total));
-    std::vector<uint8_t *> host(5 * s->world);
+    std::vector<uint8_t *> host(4 * s->world);
     for (int par = 0; par < 2; ++par)
         for (int r = 0; r < s->world; ++r) {
             host[par * s->world + r] = s->peer[r] + s->off_xw[par];
-            host[(2 + par) * s->world + r] = s->peer[r] + s->off_y[par];
+            host[(2 + par) * s->world + r] = s->peer[r] + s->off_yw[par];
         }
-    for (int r = 0; r < s->world; ++r) host[4 * s->world + r] = s->peer[r] + s->off_arrive;
     L2D_CUDA_TRY(cudaMemcpy(s->tables, host.data(), host.size() * sizeof(void *), cudaMemcpyHostToDevice));
-    L2D_CUDA_TRY(cudaMemcpy(tab_rows_of(s), rows_of.data(), rows_of.size() * sizeof(unsigned long long),
-                            cudaMemcpyHostToDevice));
     s->connected = true;
     return L2D_OK;
 }
@@ -327,13 +317,14 @@ int l2d_gemv_sharded(l2d_plan *plan, l2d_shard *s, int mode, void *stream, int *
         GemvArgs *a = reinterpret_cast<GemvArgs *>(buf.data());
         bool split = false;
         const l2d_gemv_desc &d = plan_desc(plan);
-        int st = build_args(plan, d.A, s->base + s->off_x[par], s->base + s->off_y[par] + sh.y_shard_off, mode, a,
-                            &split);
+        int st = build_args(plan, d.A, s->base + s->off_x[par], s->base + s->off_y[par] + s->row0 * s->eb_out, mode,
+                            a, &split);
         if (st == L2D_OK) st = shard_fill_args(a, sh);
         if (st == L2D_OK) st = launch_args(plan, *a, split, stream);
         if (st != L2D_OK) return st;
     } else if (s->world > 1) {
-        shard::k_shard_idle<<<shard::kIdleCtas, 32, 0, cs>>>(sh, s->base + s->off_x[par]);
+        shard::k_shard_idle<<<shard::kIdleCtas, 256, 0, cs>>>(sh, s->base + s->off_x[par], s->base + s->off_y[par],
+                                                            s->eb_out);
         L2D_CUDA_TRY(cudaGetLastError());
     }
     s->epoch = e;  // only a launched step advances the step number (all ranks must stay in step)
