@@ -172,7 +172,14 @@ typedef struct {
     int flags;          /* L2D_PLAN_* */
 } l2d_gemv_desc;
 
-enum { L2D_PLAN_NO_PROBE = 1 /* skip the domain probes: only L2D_MODE_STREAM is available */ };
+enum {
+    L2D_PLAN_NO_PROBE = 1, /* skip the domain probes: only L2D_MODE_STREAM is available */
+    L2D_PLAN_TMA = 2,      /* use the granule-ring kernels (A streamed by TMA bulk copies into per-warp
+                              shared-memory rings) for every mode when the shape allows them (rows on
+                              4 KiB boundaries, x in shared memory); by default the plan picks them
+                              per call where they were measured faster */
+    L2D_PLAN_NO_TMA = 4    /* never use the granule-ring kernels */
+};
 
 typedef struct {
     int num_sm;
@@ -193,6 +200,8 @@ typedef struct {
     size_t scratch_bytes;        /* device scratch the plan owns */
     uint64_t fallback_slots;     /* slots processed away from their home SM so far */
     uint64_t calls;              /* completed kernel calls (device epoch) */
+    int tma;                     /* granule-ring kernels: 0 unavailable, 1 picked per call, 2 every call */
+    uint64_t device_errors;      /* bit 0: a granule-ring wait ran out of time (never expected) */
 } l2d_plan_stats;
 
 /* Creates a plan.  map == NULL probes the device and desc->A's region (2 MiB pages covering

@@ -63,6 +63,8 @@ struct GemvArgs {
     int dom_kind;                 // 0 = probed XOR model, 1 = hash of the granule index
     int flip;                     // 1 = swapped control
     int x_smem;                   // 1 = stage the slot's x vectors in shared memory
+    int ring_off;                 // TMA kernels: byte offset of the granule rings in dynamic shared memory
+    int use_tma;                  // 1 = this call runs the granule-ring kernel
     const int32_t *sm_slot;       // [kMaxSmid] slot of each SM, -1 = none
     int n_slots;
     int n_dom0;
@@ -89,7 +91,7 @@ struct GemvArgs {
     uint32_t *shard_status;             // bit 0: x never arrived, bit 1: a peer's rows never arrived
     uint64_t shard_timeout_ns;
     unsigned long long *claim;    // [n_slots] epoch of the last claim
-    unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims
+    unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims, [3] bit 0: a ring wait timed out
 };
 
 struct Vec32 {
@@ -453,6 +455,242 @@ __device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int
     __syncthreads();
 }
 
+// ---------------------------------------------------------------------------------------------
+// TMA ring variant (kernels with TMA = true; used when every row starts on a 4 KiB granule and x
+// is staged in shared memory).  A reaches shared memory through cp.async.bulk, one 4 KiB granule
+// per stage and kTmaStages stages per warp, each completed on its own mbarrier.  Lane 0 of every
+// warp is the producer: it walks the warp's rows -- for a split row only the granules of its
+// group's domain -- and keeps kTmaStages granules in flight across row boundaries, so the memory
+// pipeline never drains between row visits and holds no registers.  All 32 lanes consume a stage:
+// lane l takes bytes [16 l, 16 l + 16) and [512 + 16 l, ...) of each 1 KiB unit, from A's stage
+// and from the staged x (bank-conflict-free 16-byte shared loads).
+// ---------------------------------------------------------------------------------------------
+#ifndef L2D_TMA_WARPS
+#define L2D_TMA_WARPS 16
+#endif
+#ifndef L2D_TMA_STAGES
+#define L2D_TMA_STAGES 2
+#endif
+constexpr int kTmaWarps = L2D_TMA_WARPS;  // consumer warps per CTA (lane 0 of each is its producer)
+constexpr int kTmaThreads = kTmaWarps * 32;
+constexpr int kTmaStages = L2D_TMA_STAGES;  // 4 KiB granules in flight per warp
+constexpr int kGranShift = 12;
+constexpr int kGranBytes = 1 << kGranShift;
+constexpr size_t kTmaRingBytes = static_cast<size_t>(kTmaWarps) * kTmaStages * kGranBytes;
+// Ring block: granules, then one mbarrier and one meta record per stage.
+constexpr size_t kTmaBarOff = kTmaRingBytes;
+constexpr size_t kTmaMetaOff = kTmaBarOff + static_cast<size_t>(kTmaWarps) * kTmaStages * 8;
+constexpr size_t kTmaBlockBytes = kTmaMetaOff + static_cast<size_t>(kTmaWarps) * kTmaStages * 16;
+
+struct TmaMeta {
+    int row;   // row of the granule (-1: the producer had nothing left for this stage)
+    int xoff;  // byte offset of the granule's x in the staged x
+    int last;  // bit 0: the row's last granule for this group; bit 1: a spill row (whole row here)
+    int pad;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_to_smem(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// The warp's walk over its rows of a slot, one granule at a time.  All 32 lanes run it in step:
+// when a row starts, lane l evaluates granule l's domain and one ballot gives the row's granules in
+// this group's domain (rows hold at most 32 granules: x fits in shared memory); each further
+// granule is the next bit of that mask.  Lane 0 records the stage's meta and starts its copy.
+struct TmaProducer {
+    RowIter it;
+    int64_t row, r1;
+    int32_t step_phase;
+    int G;              // granules per row
+    uint32_t mask;      // granules of the current row still to fetch
+    bool spill_row;
+    const uint8_t *rowp;
+    int xbase;
+
+    template <bool SPLIT>
+    __device__ __forceinline__ bool next(const GemvArgs &a, int grp, bool small_grp, int nwarps, int lane,
+                                         const uint8_t *xs, int64_t b0, uint8_t *stage, uint64_t *bar, TmaMeta *meta) {
+        while (mask == 0u) {
+            if (row >= r1) return false;
+            const bool spill = SPLIT && it.spill(a);
+            if (!(spill && small_grp)) {
+                spill_row = spill;
+                rowp = a.A + static_cast<int64_t>(it.b) * a.stride_a_bytes + static_cast<int64_t>(it.i) * a.lda_bytes;
+                xbase = xs ? static_cast<int>((it.b - b0) * ((a.row_bytes + 15) & ~int64_t(15))) : 0;
+                bool own = lane < G;
+                if (SPLIT && !spill && own) {
+                    const uint64_t u = (static_cast<uint64_t>(rowp - a.region_base) >> kUnitShift) +
+                                       (static_cast<uint64_t>(lane) << (kGranShift - kUnitShift));
+                    own = unit_dom(a, u) == grp;
+                }
+                mask = __ballot_sync(0xffffffffu, own);
+                if (mask != 0u) break;
+                if (SPLIT && lane == 0) a.part[grp * a.rows_total + row] = 0.0f;  // no granule of ours
+            }
+            row += nwarps;
+            it.advance(a, nwarps, step_phase);
+        }
+        const int g = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        if (lane == 0) {
+            meta->row = static_cast<int>(row);
+            meta->xoff = xbase + g * kGranBytes;
+            meta->last = (mask == 0u ? 1 : 0) | (spill_row ? 2 : 0);
+            mbar_expect_tx(bar, kGranBytes);
+            bulk_to_smem(stage, rowp + static_cast<int64_t>(g) * kGranBytes, kGranBytes, bar);
+        }
+        if (mask == 0u) {
+            row += nwarps;
+            it.advance(a, nwarps, step_phase);
+        }
+        return true;
+    }
+};
+
+// Stages each warp has consumed so far in this launch: stage c % kTmaStages is used for the c-th
+// granule and its barrier completes phase c / kTmaStages, also across the slots of one CTA.
+__shared__ int s_tma_count[kTmaWarps];
+
+template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
+__device__ __forceinline__ void run_slot_tma(const GemvArgs &a, int slot, int warp, int nwarps, int lane,
+                                             uint8_t *smem) {
+    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    int grp = 0, idx = slot, n_group = a.n_slots;
+    if (SPLIT) {
+        grp = slot >= a.n_dom0;
+        idx = grp ? slot - a.n_dom0 : slot;
+        n_group = grp ? a.n_dom1 : a.n_dom0;
+    }
+    const int64_t r0 = a.rows_total * idx / n_group;
+    const int64_t r1 = a.rows_total * (idx + 1) / n_group;
+    if (r0 >= r1) return;
+    const uint8_t *xs = smem;
+    int64_t b0 = 0;
+    if (!SH) {
+        b0 = r0 / a.M;
+        stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
+    }
+    uint8_t *ring = smem + a.ring_off;
+    uint8_t *stages = ring + static_cast<size_t>(warp) * kTmaStages * kGranBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kTmaBarOff) + warp * kTmaStages;
+    TmaMeta *metas = reinterpret_cast<TmaMeta *>(ring + kTmaMetaOff) + warp * kTmaStages;
+    const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
+
+    const int c0 = s_tma_count[warp];
+    TmaProducer prod;
+    prod.row = r0 + warp;
+    prod.r1 = r1;
+    prod.step_phase = a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
+    prod.G = static_cast<int>(a.row_bytes >> kGranShift);
+    prod.mask = 0u;
+    if (prod.row < r1) prod.it.start(a, static_cast<int32_t>(prod.row));
+    for (int k = 0; k < kTmaStages; ++k) {
+        const int s = (c0 + k) % kTmaStages;
+        if (!prod.next<SPLIT>(a, grp, small_grp, nwarps, lane, xs, b0, stages + s * kGranBytes, bars + s, metas + s) &&
+            lane == 0)
+            metas[s].row = -1;
+    }
+    __syncwarp();
+
+    Acc<DT_IN> acc;
+    bool timed_out = false;
+    int c = c0;
+    for (;; ++c) {
+        const int s = c % kTmaStages;
+        const TmaMeta m = metas[s];
+        if (m.row < 0) break;
+        const uint32_t parity = static_cast<uint32_t>(c / kTmaStages) & 1u;
+        if (!mbar_try_wait(bars + s, parity)) {
+            const uint64_t deadline = dev::globaltimer_ns() + 1000000000ull;
+            while (!mbar_try_wait(bars + s, parity)) {
+                if (dev::globaltimer_ns() > deadline) {
+                    timed_out = true;
+                    break;
+                }
+            }
+        }
+        const uint8_t *st = stages + s * kGranBytes;
+        const uint8_t *xg = xs + m.xoff;
+#pragma unroll
+        for (int u = 0; u < kGranBytes >> kUnitShift; ++u) {
+            const int o = (u << kUnitShift) + lane * 16;
+            const uint4 a0 = *reinterpret_cast<const uint4 *>(st + o);
+            const uint4 a1 = *reinterpret_cast<const uint4 *>(st + o + 512);
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(xg + o);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(xg + o + 512);
+            Vec32 av;
+            av.v[0] = a0.x, av.v[1] = a0.y, av.v[2] = a0.z, av.v[3] = a0.w;
+            av.v[4] = a1.x, av.v[5] = a1.y, av.v[6] = a1.z, av.v[7] = a1.w;
+            acc.unit(av, x0, x1);
+        }
+        if (m.last & 1) {
+            float sum = acc.total();
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                const int64_t row = m.row;
+                if (SPLIT) {
+                    a.part[grp * a.rows_total + row] = sum;
+                    if (m.last & 2) a.part[(grp ^ 1) * a.rows_total + row] = 0.0f;
+                } else {
+                    const int64_t b = row / a.M, i = row - b * a.M;
+                    uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
+                    store_out<DT_OUT>(yp, sum);
+                    final_to_peers<DT_OUT, SH>(a, row, sum);
+                }
+            }
+            acc = Acc<DT_IN>();
+        }
+        __syncwarp();  // every lane is done with stage s before it is refilled
+        if (!prod.next<SPLIT>(a, grp, small_grp, nwarps, lane, xs, b0, stages + s * kGranBytes, bars + s, metas + s) &&
+            lane == 0)
+            metas[s].row = -1;
+        __syncwarp();
+    }
+    if (timed_out) atomicOr(a.ctl + 3, 1ull);
+    if (lane == 0) {
+        s_tma_count[warp] = c;  // the stage at c was never filled: the next slot starts there
+        __threadfence();
+    }
+    __syncthreads();
+    if (SPLIT) meet_and_combine<DT_OUT, SH>(a, grp, idx, r0, r1);
+}
+
+// Every warp's stage barriers, once per CTA, before the first copy.
+template <bool TMA> __device__ __forceinline__ void tma_init(const GemvArgs &a, uint8_t *smem) {
+    if (!TMA) return;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.ring_off + kTmaBarOff);
+    for (int k = threadIdx.x; k < kTmaWarps * kTmaStages; k += blockDim.x) mbar_init(bars + k);
+    for (int w = threadIdx.x; w < kTmaWarps; w += blockDim.x) s_tma_count[w] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+}
+
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
 __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, int nwarps, int lane, uint8_t *smem) {
     int grp = 0, idx = slot, n_group = a.n_slots;
@@ -604,7 +842,7 @@ __device__ __forceinline__ int warp_claim_any(const GemvArgs &a, unsigned long l
     return -1;
 }
 
-template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
+template <int DT_IN, int DT_OUT, bool SPLIT, bool SH, bool TMA>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int s_slot;
@@ -633,8 +871,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         }
     }
     __syncthreads();
+    tma_init<TMA>(a, smem);
     shard_stage_x<SH>(a, smem);
-    if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
+    if (s_slot >= 0) {
+        if (TMA) {
+            run_slot_tma<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
+        } else {
+            run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
+        }
+    }
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -656,7 +901,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     const int n_left = s_count;
     if (tid == 0 && n_left) atomicAdd(a.ctl + 2, static_cast<unsigned long long>(n_left));
     for (int k = 0; k < n_left; ++k) {
-        run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
+        if (TMA) {
+            run_slot_tma<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
+        } else {
+            run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
+        }
         __syncthreads();
     }
     shard_gather<DT_OUT, SH>(a);
@@ -669,25 +918,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
 
 using KernelFn = void (*)(GemvArgs);
 
-// SH: the peer-memory sharded variant (its bookkeeping is compiled out of the others).
-template <int DI, int DO> KernelFn pick_split(bool split, bool sh) {
-    if (sh) return split ? k_gemv<DI, DO, true, true> : k_gemv<DI, DO, false, true>;
-    return split ? k_gemv<DI, DO, true, false> : k_gemv<DI, DO, false, false>;
+// SH: the peer-memory sharded variant (its bookkeeping is compiled out of the others); TMA: the
+// granule-ring variant.
+template <int DI, int DO, bool TMA> KernelFn pick_split(bool split, bool sh) {
+    if (sh) return split ? k_gemv<DI, DO, true, true, TMA> : k_gemv<DI, DO, false, true, TMA>;
+    return split ? k_gemv<DI, DO, true, false, TMA> : k_gemv<DI, DO, false, false, TMA>;
 }
 
-template <int DI> KernelFn pick_out(int dout, bool split, bool sh) {
+template <int DI> KernelFn pick_out(int dout, bool split, bool sh, bool tma) {
     switch (dout) {
-    case L2D_F32: return pick_split<DI, L2D_F32>(split, sh);
-    case L2D_F16: return pick_split<DI, L2D_F16>(split, sh);
-    default: return pick_split<DI, L2D_BF16>(split, sh);
+    case L2D_F32: return tma ? pick_split<DI, L2D_F32, true>(split, sh) : pick_split<DI, L2D_F32, false>(split, sh);
+    case L2D_F16: return tma ? pick_split<DI, L2D_F16, true>(split, sh) : pick_split<DI, L2D_F16, false>(split, sh);
+    default: return tma ? pick_split<DI, L2D_BF16, true>(split, sh) : pick_split<DI, L2D_BF16, false>(split, sh);
     }
 }
 
-KernelFn pick_kernel(int din, int dout, bool split, bool sh = false) {
+KernelFn pick_kernel(int din, int dout, bool split, bool sh = false, bool tma = false) {
     switch (din) {
-    case L2D_F32: return pick_out<L2D_F32>(dout, split, sh);
-    case L2D_F16: return pick_out<L2D_F16>(dout, split, sh);
-    default: return pick_out<L2D_BF16>(dout, split, sh);
+    case L2D_F32: return pick_out<L2D_F32>(dout, split, sh, tma);
+    case L2D_F16: return pick_out<L2D_F16>(dout, split, sh, tma);
+    default: return pick_out<L2D_BF16>(dout, split, sh, tma);
     }
 }
 
@@ -801,6 +1051,9 @@ struct l2d_plan {
     float *d_part = nullptr;
     unsigned int *d_meet = nullptr;
     size_t x_smem_bytes = 0;  // dynamic shared memory holding the x vectors (0 = read x through L1)
+    bool tma = false;         // granule-ring kernels are available (TMA bulk copies of A)
+    bool tma_force = false;   // L2D_PLAN_TMA: use them for every mode
+    size_t ring_off = 0;      // their ring block's offset in dynamic shared memory
     unsigned long long *d_claim = nullptr;
     unsigned long long *d_ctl = nullptr;
 };
@@ -1013,8 +1266,22 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
         if (max_nb * rb16 <= kXSmemMax) p->x_smem_bytes = static_cast<size_t>(max_nb * rb16);
     }
-    for (int v = 0; v < 4; ++v) {
-        const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, v & 1, v >> 1), d.device);
+    // Granule-ring kernels: every row must start on a 4 KiB granule, x must sit in shared memory next
+    // to the rings, and the domain model must not split a granule.
+    if (!(d.flags & L2D_PLAN_NO_TMA) && p->x_smem_bytes > 0 && !(reinterpret_cast<uintptr_t>(d.A) & (kGranBytes - 1)) &&
+        (d.N * eb) % kGranBytes == 0 && (d.lda * eb) % kGranBytes == 0 &&
+        (d.batch == 1 || (d.stride_a * eb) % kGranBytes == 0) && (!p->has_domains || p->gran_shift >= kGranShift)) {
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device);
+        const size_t ring_off = (p->x_smem_bytes + 1023) & ~size_t(1023);
+        if (ring_off + kTmaBlockBytes + 8 * 1024 <= static_cast<size_t>(optin)) {
+            p->tma = true;
+            p->tma_force = (d.flags & L2D_PLAN_TMA) != 0;
+            p->ring_off = ring_off;
+        }
+    }
+    for (int v = 0; v < 8; ++v) {
+        const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, v & 1, (v >> 1) & 1, v >> 2), d.device);
         if (fe != L2D_OK) {
             cudaFree(p->dev_block);
             delete p;
@@ -1081,6 +1348,15 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.claim = p->d_claim;
     a.ctl = p->d_ctl;
     a.x_smem = p->x_smem_bytes > 0;
+    a.ring_off = static_cast<int>(p->ring_off);
+    // Kernel choice, measured on B200: the rings win wherever the register pipeline's drain between
+    // row visits shows (split calls up to ~2 GiB of A, or with rows of <= 16 KiB; unsplit calls
+    // below 1 GiB); on larger, HBM-saturating calls the register kernels keep a 1-4 % edge.
+    if (p->tma) {
+        const int64_t a_bytes = p->rows_total * a.row_bytes;
+        a.use_tma = p->tma_force ||
+                    (split ? (a_bytes < (int64_t(2) << 30) || a.row_bytes <= 16 * 1024) : a_bytes < (int64_t(1) << 30));
+    }
     // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes a
     // fraction (n_big - n_small)/(n_big + n_small) of the rows whole, spread evenly, so every SM
     // streams the same bytes.  The swapped control stays pure (no spill rows).
@@ -1111,11 +1387,15 @@ int check_args(const GemvArgs &a) {
 int launch_args(l2d_plan *p, const GemvArgs &a, bool split, void *stream) {
     const int chk = check_args(a);
     if (chk != L2D_OK) return chk;
-    KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split, a.shard_world > 1);
+    KernelFn k = pick_kernel(p->desc.dtype_in, p->desc.dtype_out, split, a.shard_world > 1, a.use_tma != 0);
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != p->device) cudaSetDevice(p->device);
-    k<<<p->n_slots, kThreads, p->x_smem_bytes, static_cast<cudaStream_t>(stream)>>>(a);
+    if (a.use_tma) {
+        k<<<p->n_slots, kTmaThreads, p->ring_off + kTmaBlockBytes, static_cast<cudaStream_t>(stream)>>>(a);
+    } else {
+        k<<<p->n_slots, kThreads, p->x_smem_bytes, static_cast<cudaStream_t>(stream)>>>(a);
+    }
     cudaError_t e = cudaGetLastError();
     if (prev >= 0 && prev != p->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
@@ -1174,7 +1454,8 @@ int l2d_plan_stats_get(l2d_plan *p, l2d_plan_stats *s) {
     s->domain_sms[0] = p->n_dom[0];
     s->domain_sms[1] = p->n_dom[1];
     s->grid = p->n_slots;
-    s->block = kThreads;
+    s->block = p->tma ? kTmaThreads : kThreads;
+    s->tma = p->tma ? (p->tma_force ? 2 : 1) : 0;
     s->scratch_bytes = p->dev_bytes;
     int prev = -1;
     cudaGetDevice(&prev);
@@ -1186,6 +1467,7 @@ int l2d_plan_stats_get(l2d_plan *p, l2d_plan_stats *s) {
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "plan_stats: %s", cudaGetErrorString(e));
     s->calls = ctl[0];
     s->fallback_slots = ctl[2];
+    s->device_errors = ctl[3];
     return L2D_OK;
 }
 

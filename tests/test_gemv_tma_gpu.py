@@ -1,0 +1,137 @@
+"""GPU parity of the granule-ring (TMA bulk copy) kernels, plans made with L2D_PLAN_TMA.
+
+Same bars as the register kernels: fp32 relative L2 <= 1e-5 and fp16/bf16 <= 2e-3 against the fp64
+oracle (of the same rounded inputs, rounded to the output type); the exact-integer inputs
+bit-exact; AWARE and SWAPPED bit-identical on split rows; repeated calls bit-identical.  A shape
+the ring kernels cannot take (rows off the 4 KiB granules) falls back to the register kernels.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import l2domain_b200 as L  # noqa: E402
+import oracle as O  # noqa: E402
+
+GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_pins.json")))
+TOL = {L.F32: 1e-5, L.F16: 2e-3, L.BF16: 2e-3}
+ALL_MODES = [L.MODE_OBLIVIOUS, L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_STREAM]
+PAGE = 2 * 1024 * 1024
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    torch.cuda.set_device(0)
+    return torch.device("cuda", 0)
+
+
+def to_dev(a):
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def inputs(M, N, dtype, batch=1, kind="cfg"):
+    if kind == "int":
+        A32 = O.ref_fill(batch * M * N, 4242, 0, integer_mode=True)
+        x32 = O.ref_fill(batch * N, 4242, 1, integer_mode=True)
+    else:
+        A32 = O.cfg_fill(batch * M * N, 0, 0, O.NORMAL, 0.0, 0.02)
+        x32 = O.cfg_fill(batch * N, 0, 1, O.NORMAL, 0.0, 1.0)
+    return O.round_to(A32, dtype), O.round_to(x32, dtype)
+
+
+def run(A_h, x_h, M, N, dtype, dtype_out, modes, batch=1, tma=True):
+    nbytes = A_h.nbytes
+    raw = torch.empty(nbytes + PAGE, dtype=torch.uint8, device="cuda")
+    off = (-raw.data_ptr()) % PAGE
+    A = raw[off: off + nbytes]
+    A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
+    x = to_dev(x_h)
+    plan = L.GemvPlan(A, M, N, dtype, dtype_out, batch=batch, tma=tma)
+    outs = {}
+    for mode in modes:
+        if dtype_out == L.F32:
+            y = torch.full((batch * M,), float("nan"), dtype=torch.float32, device="cuda")
+        else:
+            y = torch.full((batch * M,), -1, dtype=torch.int16, device="cuda")
+        plan.gemv(A, x, y, mode)
+        torch.cuda.synchronize()
+        yh = y.cpu().numpy()
+        outs[mode] = yh if dtype_out == L.F32 else O.widen(yh.view(np.uint16), dtype_out)
+    stats = plan.stats()
+    plan.close()
+    return outs, stats
+
+
+def oracle(A, x, dtype, M, N, batch, dtype_out):
+    ys = [O.gemv_f64(A[b * M * N:(b + 1) * M * N], x[b * N:(b + 1) * N], dtype, M, N, N) for b in range(batch)]
+    y = np.concatenate(ys)
+    return O.round_out(y, dtype_out) if dtype_out != L.F32 else y
+
+
+@pytest.mark.parametrize("M,N,dtype,dtype_out,batch", [
+    (3000, 4096, L.F16, L.F16, 1),     # 8 KiB rows: 2 granules
+    (2049, 8192, L.BF16, L.BF16, 1),   # 16 KiB rows
+    (1500, 2048, L.F32, L.F32, 1),     # 8 KiB fp32 rows
+    (513, 16384, L.F16, L.F32, 1),     # 32 KiB rows, fp32 out
+    (300, 4096, L.F16, L.F16, 3),      # batched, granule-aligned problem stride
+    (7, 2048, L.BF16, L.F32, 1),       # fewer rows than warps
+])
+def test_ring_kernels_match_oracle(dev, M, N, dtype, dtype_out, batch):
+    A, x = inputs(M, N, dtype, batch)
+    outs, stats = run(A, x, M, N, dtype, dtype_out, ALL_MODES, batch)
+    assert stats["tma"] == 2 and stats["device_errors"] == 0
+    ref = oracle(A, x, dtype, M, N, batch, dtype_out)
+    for m in ALL_MODES:
+        err = O.rel_l2(ref.astype(np.float64), outs[m])
+        assert err <= TOL[dtype], f"mode {m}: rel L2 {err:.3g}"
+
+
+def test_ring_kernels_integer_kat_bit_exact(dev):
+    g = GOLD["integer_kat"]
+    M, N = g["M"], g["K"]
+    A, x = inputs(M, N, L.F32, kind="int")
+    outs, stats = run(A, x, M, N, L.F32, L.F32, ALL_MODES)
+    assert stats["tma"] == 2
+    want = np.array(g["y"], np.float32)
+    for m in ALL_MODES:
+        assert np.array_equal(outs[m], want), f"mode {m}"
+
+
+def test_ring_kernels_aware_swapped_identical_and_deterministic(dev):
+    M, N = 1024, 8192
+    A, x = inputs(M, N, L.F16)
+    outs, stats = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_AWARE])
+    n0, n1 = stats["domain_sms"]
+    num, den = abs(n1 - n0), n0 + n1
+    split_rows = np.array([num == 0 or (r + 1) * num // den == r * num // den for r in range(M)])
+    assert np.array_equal(outs[L.MODE_AWARE][split_rows], outs[L.MODE_SWAPPED][split_rows])
+    outs2, _ = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE])
+    assert np.array_equal(outs[L.MODE_AWARE], outs2[L.MODE_AWARE])
+
+
+def test_ring_kernels_agree_with_register_kernels(dev):
+    M, N = 4096, 8192
+    A, x = inputs(M, N, L.BF16)
+    ring, s1 = run(A, x, M, N, L.BF16, L.F32, [L.MODE_AWARE], tma=True)
+    reg, s0 = run(A, x, M, N, L.BF16, L.F32, [L.MODE_AWARE], tma=False)
+    assert s1["tma"] == 2 and s0["tma"] == 0
+    a, b = ring[L.MODE_AWARE].astype(np.float64), reg[L.MODE_AWARE].astype(np.float64)
+    assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-5
+
+
+def test_unaligned_rows_fall_back_to_register_kernels(dev):
+    M, N = 500, 1000  # 2000-byte fp16 rows: not on 4 KiB granules
+    A, x = inputs(M, N, L.F16)
+    outs, stats = run(A, x, M, N, L.F16, L.F16, ALL_MODES)
+    assert stats["tma"] == 0
+    ref = oracle(A, x, L.F16, M, N, 1, L.F16)
+    for m in ALL_MODES:
+        assert O.rel_l2(ref.astype(np.float64), outs[m]) <= TOL[L.F16]
