@@ -848,7 +848,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     __shared__ int s_slot;
     __shared__ int s_last;
     __shared__ int s_count;
-    __shared__ int s_list[kMaxSmid];
+    __shared__ uint32_t s_left[kMaxSmid / 32];  // slots the last CTA claimed in its sweep (bit set)
     __shared__ unsigned long long s_epoch;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     if (warp == 0) {
@@ -869,6 +869,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
             s_epoch = E;
             s_count = 0;
         }
+        if (lane < kMaxSmid / 32) s_left[lane] = 0u;
     }
     __syncthreads();
     tma_init<TMA>(a, smem);
@@ -895,18 +896,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     // Last CTA: slots whose SM never hosted a CTA of this launch, found by one parallel sweep.
     const unsigned long long E = s_epoch;
     for (int t = tid; t < a.n_slots; t += blockDim.x) {
-        if (ld_claim(a.claim + t) < E && atomicMax(a.claim + t, E) < E) s_list[atomicAdd(&s_count, 1)] = t;
+        if (ld_claim(a.claim + t) < E && atomicMax(a.claim + t, E) < E) {
+            atomicOr(&s_left[t >> 5], 1u << (t & 31));
+            atomicAdd(&s_count, 1);
+        }
     }
     __syncthreads();
     const int n_left = s_count;
     if (tid == 0 && n_left) atomicAdd(a.ctl + 2, static_cast<unsigned long long>(n_left));
-    for (int k = 0; k < n_left; ++k) {
-        if (TMA) {
-            run_slot_tma<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
-        } else {
-            run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_list[k], warp, nwarps, lane, smem);
+    for (int w = 0; n_left && w < kMaxSmid / 32; ++w) {
+        for (uint32_t m = s_left[w]; m; m &= m - 1u) {
+            const int t = w * 32 + __ffs(m) - 1;
+            if (TMA) {
+                run_slot_tma<DT_IN, DT_OUT, SPLIT, SH>(a, t, warp, nwarps, lane, smem);
+            } else {
+                run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, t, warp, nwarps, lane, smem);
+            }
+            __syncthreads();
         }
-        __syncthreads();
     }
     shard_gather<DT_OUT, SH>(a);
     if (tid == 0) {
@@ -1274,7 +1281,7 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device);
         const size_t ring_off = (p->x_smem_bytes + 1023) & ~size_t(1023);
-        if (ring_off + kTmaBlockBytes + 8 * 1024 <= static_cast<size_t>(optin)) {
+        if (ring_off + kTmaBlockBytes + 1024 <= static_cast<size_t>(optin)) {  // static shared memory < 1 KiB
             p->tma = true;
             p->tma_force = (d.flags & L2D_PLAN_TMA) != 0;
             p->ring_off = ring_off;
