@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the cpu_baseline leg")
     ap.add_argument("--rows", type=int, default=0,
                     help="override M (a smaller case of the same row shape, for ncu captures)")
+    ap.add_argument("--kernel", choices=["auto", "ring", "register"], default="auto",
+                    help="GEMV kernels: picked per call (auto), TMA granule rings, or register pipeline")
     ap.add_argument("--no-aux", action="store_true", help="skip the per-mode and L2-resident side measurements")
     return ap.parse_args()
 
@@ -286,7 +288,8 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
 
     t_plan = time.perf_counter()
-    plan = L.GemvPlan(A, m_loc, N, dt, dt, batch=batch, device=local)
+    plan = L.GemvPlan(A, m_loc, N, dt, dt, batch=batch, device=local,
+                      tma={"auto": None, "ring": True, "register": False}[args.kernel])
     t_plan = time.perf_counter() - t_plan
     pstats = plan.stats()
 
@@ -513,7 +516,8 @@ def run_ours(args, rank, world, local):
             "plan": {"probe_and_plan_s": round(t_plan, 3), "domain_sms": pstats["domain_sms"],
                      "granule_shift": pstats["granule_shift"], "domain_bytes": pstats["domain_bytes"],
                      "split_rows": pstats["split_rows"], "fallback_slots": fstats["fallback_slots"],
-                     "calls": fstats["calls"]},
+                     "calls": fstats["calls"],
+                     "kernel": "ring (TMA bulk copies)" if fstats["ring_modes"] & (1 << L.MODE_AWARE) else "register"},
             "check": {"rows": 64, "rel_l2_vs_f64": rel, "p2p_gather_equals_nccl": gather_exact},
         }
         print(json.dumps(line), flush=True)

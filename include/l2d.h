@@ -202,6 +202,7 @@ typedef struct {
     uint64_t calls;              /* completed kernel calls (device epoch) */
     int tma;                     /* granule-ring kernels: 0 unavailable, 1 picked per call, 2 every call */
     uint64_t device_errors;      /* bit 0: a granule-ring wait ran out of time (never expected) */
+    int ring_modes;              /* bit m set: calls in mode m run the granule-ring kernels */
 } l2d_plan_stats;
 
 /* Creates a plan.  map == NULL probes the device and desc->A's region (2 MiB pages covering

@@ -1316,6 +1316,16 @@ int l2d_plan_destroy(l2d_plan *p) {
 
 namespace l2d {
 
+// Kernel choice, measured on B200: the rings win wherever the register pipeline's drain between row
+// visits shows (split calls up to ~2 GiB of A, or with rows of <= 16 KiB; unsplit calls below
+// 1 GiB); on larger, HBM-saturating calls the register kernels keep a 1-4 % edge.
+bool use_ring(const l2d_plan *p, bool split) {
+    if (!p->tma) return false;
+    if (p->tma_force) return true;
+    const int64_t row_bytes = p->desc.N * p->eb_in, a_bytes = p->rows_total * row_bytes;
+    return split ? (a_bytes < (int64_t(2) << 30) || row_bytes <= 16 * 1024) : a_bytes < (int64_t(1) << 30);
+}
+
 // Kernel arguments of one call on plan p (no sharding); *split tells which kernel variant runs.
 int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, GemvArgs *out, bool *split_out) {
     if (!p) return set_error(L2D_ERR_INVALID, "null plan");
@@ -1356,14 +1366,7 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.ctl = p->d_ctl;
     a.x_smem = p->x_smem_bytes > 0;
     a.ring_off = static_cast<int>(p->ring_off);
-    // Kernel choice, measured on B200: the rings win wherever the register pipeline's drain between
-    // row visits shows (split calls up to ~2 GiB of A, or with rows of <= 16 KiB; unsplit calls
-    // below 1 GiB); on larger, HBM-saturating calls the register kernels keep a 1-4 % edge.
-    if (p->tma) {
-        const int64_t a_bytes = p->rows_total * a.row_bytes;
-        a.use_tma = p->tma_force ||
-                    (split ? (a_bytes < (int64_t(2) << 30) || a.row_bytes <= 16 * 1024) : a_bytes < (int64_t(1) << 30));
-    }
+    a.use_tma = use_ring(p, split) ? 1 : 0;
     // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes a
     // fraction (n_big - n_small)/(n_big + n_small) of the rows whole, spread evenly, so every SM
     // streams the same bytes.  The swapped control stays pure (no spill rows).
@@ -1463,6 +1466,9 @@ int l2d_plan_stats_get(l2d_plan *p, l2d_plan_stats *s) {
     s->grid = p->n_slots;
     s->block = p->tma ? kTmaThreads : kThreads;
     s->tma = p->tma ? (p->tma_force ? 2 : 1) : 0;
+    s->ring_modes = 0;
+    for (int m = L2D_MODE_OBLIVIOUS; m <= L2D_MODE_STREAM; ++m)
+        if (use_ring(p, m != L2D_MODE_STREAM && p->desc.N > 0)) s->ring_modes |= 1 << m;
     s->scratch_bytes = p->dev_bytes;
     int prev = -1;
     cudaGetDevice(&prev);
