@@ -203,6 +203,8 @@ typedef struct {
     int tma;                     /* granule-ring kernels: 0 unavailable, 1 picked per call, 2 every call */
     uint64_t device_errors;      /* bit 0: a granule-ring wait ran out of time (never expected) */
     int ring_modes;              /* bit m set: calls in mode m run the granule-ring kernels */
+    int64_t ring_whole_rows;     /* ring calls in AWARE / OBLIVIOUS: the last rows, taken whole by either group */
+    int64_t ring_chunk_rows;     /* ring calls: rows per claim from a row pool */
 } l2d_plan_stats;
 
 /* Creates a plan.  map == NULL probes the device and desc->A's region (2 MiB pages covering

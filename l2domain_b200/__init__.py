@@ -81,7 +81,8 @@ class PlanStats(C.Structure):
     _fields_ = [("rows_total", C.c_int64), ("granule_shift", C.c_int), ("domain_bytes", C.c_int64 * 2),
                 ("split_rows", C.c_int64), ("domain_sms", C.c_int * 2), ("grid", C.c_int), ("block", C.c_int),
                 ("scratch_bytes", C.c_size_t), ("fallback_slots", C.c_uint64), ("calls", C.c_uint64),
-                ("tma", C.c_int), ("device_errors", C.c_uint64), ("ring_modes", C.c_int)]
+                ("tma", C.c_int), ("device_errors", C.c_uint64), ("ring_modes", C.c_int),
+                ("ring_whole_rows", C.c_int64), ("ring_chunk_rows", C.c_int64)]
 
 
 # Every symbol include/l2d.h declares, with its ctypes signature.

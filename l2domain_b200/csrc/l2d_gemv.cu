@@ -24,6 +24,10 @@
 //    claimed with a per-call epoch: a CTA whose SM slot is already taken takes any unclaimed slot,
 //    and the last CTA to finish processes slots nobody claimed, so every row is computed exactly
 //    once whatever the block scheduler does.  Nothing in the kernel waits on another CTA.
+//  * The granule-ring kernels (batch 1, rows on 4 KiB granules; the default wherever they apply)
+//    stream A into shared memory with TMA bulk copies and replace the slots by row pools that warps
+//    claim a chunk at a time, so SMs that get less bandwidth take fewer rows.  A split row's two
+//    partials meet in one 64-bit exchange word per row (see walk_pools).
 #include "l2d_device.cuh"
 #include "l2d_internal.h"
 
@@ -32,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -58,6 +63,7 @@ struct GemvArgs {
     int64_t rows_total;
     const uint8_t *region_base;   // 1 KiB aligned (2 MiB aligned when the attr table is used)
     const uint32_t *attr_bits;    // per 2 MiB page of the region, 32 pages per word
+    int64_t attr_words;           // words in attr_bits
     uint32_t mask;
     int gran_shift;
     int dom_kind;                 // 0 = probed XOR model, 1 = hash of the granule index
@@ -74,6 +80,11 @@ struct GemvArgs {
     int big_grp;                  // the group with more SMs
     float *part;                  // [2][rows_total] each domain group's partial of each row (split calls)
     unsigned int *meet;           // [n_slots] arrivals per interval of the two groups' slot partitions, zero between calls
+    unsigned long long *xch;      // ring kernels: [rows_total] a split row's first partial and its call's tag (0 = empty)
+    int64_t whole_lo;             // ring kernels: rows [whole_lo, rows_total) form the whole-row pool
+    int64_t pool_chunk;           // ring kernels: rows per pool claim
+    int first_chunks[2];          // ring kernels: chunks in the first claim of a group-g CTA (group 0: unsplit)
+    uint32_t grp_bits[kMaxSmid / 32];  // ring kernels: bit s set = SM s belongs to domain group 1
     // Peer-memory row sharding (shard_world > 1; batch 1).  Every exchange is a flagged 8-byte
     // word (4 bytes of data, the step number) stored into a peer's buffer; a reader retries a word
     // until its flag carries the step, so nothing on the way needs a fence or a counter.  Rank 0's
@@ -91,7 +102,8 @@ struct GemvArgs {
     uint32_t *shard_status;             // bit 0: x never arrived, bit 1: a peer's rows never arrived
     uint64_t shard_timeout_ns;
     unsigned long long *claim;    // [n_slots] epoch of the last claim
-    unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims, [3] bit 0: a ring wait timed out
+    unsigned long long *ctl;      // [0] epoch, [1] CTAs done, [2] fallback claims, [3] bit 0: a ring wait timed out,
+                                  // [16] [32] [48] ring pool counters (64 words, zero between calls)
 };
 
 struct Vec32 {
@@ -459,9 +471,9 @@ __device__ __forceinline__ void meet_and_combine(const GemvArgs &a, int grp, int
 // TMA ring variant (kernels with TMA = true; used when every row starts on a 4 KiB granule and x
 // is staged in shared memory).  A reaches shared memory through cp.async.bulk, one 4 KiB granule
 // per stage and kTmaStages stages per warp, each completed on its own mbarrier.  Lane 0 of every
-// warp is the producer: it walks the warp's rows -- for a split row only the granules of its
-// group's domain -- and keeps kTmaStages granules in flight across row boundaries, so the memory
-// pipeline never drains between row visits and holds no registers.  All 32 lanes consume a stage:
+// warp is the producer: it walks the rows the warp claims -- for a split row only the granules of
+// its group's domain -- and keeps kTmaStages granules in flight across row boundaries, so the
+// memory pipeline never drains between row visits and holds no registers.  All 32 lanes consume a stage:
 // lane l takes bytes [16 l, 16 l + 16) and [512 + 16 l, ...) of each 1 KiB unit, from A's stage
 // and from the staged x (bank-conflict-free 16-byte shared loads).
 // ---------------------------------------------------------------------------------------------
@@ -516,179 +528,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
-}
-
-// The warp's walk over its rows of a slot, one granule at a time.  All 32 lanes run it in step:
-// when a row starts, lane l evaluates granule l's domain and one ballot gives the row's granules in
-// this group's domain (rows hold at most 32 granules: x fits in shared memory); each further
-// granule is the next bit of that mask.  Lane 0 records the stage's meta and starts its copy.
-struct TmaProducer {
-    RowIter it;
-    int64_t row, r1;
-    int32_t step_phase;
-    int G;              // granules per row
-    uint32_t mask;      // granules of the current row still to fetch
-    bool spill_row;
-    const uint8_t *rowp;
-    int xbase;
-
-    template <bool SPLIT>
-    __device__ __forceinline__ bool next(const GemvArgs &a, int grp, bool small_grp, int nwarps, int lane,
-                                         const uint8_t *xs, int64_t b0, uint8_t *stage, uint64_t *bar, TmaMeta *meta) {
-        while (mask == 0u) {
-            if (row >= r1) return false;
-            const bool spill = SPLIT && it.spill(a);
-            if (!(spill && small_grp)) {
-                spill_row = spill;
-                rowp = a.A + static_cast<int64_t>(it.b) * a.stride_a_bytes + static_cast<int64_t>(it.i) * a.lda_bytes;
-                xbase = xs ? static_cast<int>((it.b - b0) * ((a.row_bytes + 15) & ~int64_t(15))) : 0;
-                bool own = lane < G;
-                if (SPLIT && !spill && own) {
-                    const uint64_t u = (static_cast<uint64_t>(rowp - a.region_base) >> kUnitShift) +
-                                       (static_cast<uint64_t>(lane) << (kGranShift - kUnitShift));
-                    own = unit_dom(a, u) == grp;
-                }
-                mask = __ballot_sync(0xffffffffu, own);
-                if (mask != 0u) break;
-                if (SPLIT && lane == 0) a.part[grp * a.rows_total + row] = 0.0f;  // no granule of ours
-            }
-            row += nwarps;
-            it.advance(a, nwarps, step_phase);
-        }
-        const int g = __ffs(mask) - 1;
-        mask &= mask - 1u;
-        if (lane == 0) {
-            meta->row = static_cast<int>(row);
-            meta->xoff = xbase + g * kGranBytes;
-            meta->last = (mask == 0u ? 1 : 0) | (spill_row ? 2 : 0);
-            mbar_expect_tx(bar, kGranBytes);
-            bulk_to_smem(stage, rowp + static_cast<int64_t>(g) * kGranBytes, kGranBytes, bar);
-        }
-        if (mask == 0u) {
-            row += nwarps;
-            it.advance(a, nwarps, step_phase);
-        }
-        return true;
-    }
-};
-
-// Stages each warp has consumed so far in this launch: stage c % kTmaStages is used for the c-th
-// granule and its barrier completes phase c / kTmaStages, also across the slots of one CTA.
-__shared__ int s_tma_count[kTmaWarps];
-
-template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
-__device__ __forceinline__ void run_slot_tma(const GemvArgs &a, int slot, int warp, int nwarps, int lane,
-                                             uint8_t *smem) {
-    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
-    int grp = 0, idx = slot, n_group = a.n_slots;
-    if (SPLIT) {
-        grp = slot >= a.n_dom0;
-        idx = grp ? slot - a.n_dom0 : slot;
-        n_group = grp ? a.n_dom1 : a.n_dom0;
-    }
-    const int64_t r0 = a.rows_total * idx / n_group;
-    const int64_t r1 = a.rows_total * (idx + 1) / n_group;
-    if (r0 >= r1) return;
-    const uint8_t *xs = smem;
-    int64_t b0 = 0;
-    if (!SH) {
-        b0 = r0 / a.M;
-        stage_x(a, smem, b0, (r1 - 1) / a.M - b0 + 1);
-    }
-    uint8_t *ring = smem + a.ring_off;
-    uint8_t *stages = ring + static_cast<size_t>(warp) * kTmaStages * kGranBytes;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kTmaBarOff) + warp * kTmaStages;
-    TmaMeta *metas = reinterpret_cast<TmaMeta *>(ring + kTmaMetaOff) + warp * kTmaStages;
-    const bool small_grp = SPLIT && a.spill_num != 0 && grp != a.big_grp;
-
-    const int c0 = s_tma_count[warp];
-    TmaProducer prod;
-    prod.row = r0 + warp;
-    prod.r1 = r1;
-    prod.step_phase = a.spill_num ? static_cast<int32_t>(static_cast<int64_t>(nwarps) * a.spill_num % a.spill_den) : 0;
-    prod.G = static_cast<int>(a.row_bytes >> kGranShift);
-    prod.mask = 0u;
-    if (prod.row < r1) prod.it.start(a, static_cast<int32_t>(prod.row));
-    for (int k = 0; k < kTmaStages; ++k) {
-        const int s = (c0 + k) % kTmaStages;
-        if (!prod.next<SPLIT>(a, grp, small_grp, nwarps, lane, xs, b0, stages + s * kGranBytes, bars + s, metas + s) &&
-            lane == 0)
-            metas[s].row = -1;
-    }
-    __syncwarp();
-
-    Acc<DT_IN> acc;
-    bool timed_out = false;
-    int c = c0;
-    for (;; ++c) {
-        const int s = c % kTmaStages;
-        const TmaMeta m = metas[s];
-        if (m.row < 0) break;
-        const uint32_t parity = static_cast<uint32_t>(c / kTmaStages) & 1u;
-        if (!mbar_try_wait(bars + s, parity)) {
-            const uint64_t deadline = dev::globaltimer_ns() + 1000000000ull;
-            while (!mbar_try_wait(bars + s, parity)) {
-                if (dev::globaltimer_ns() > deadline) {
-                    timed_out = true;
-                    break;
-                }
-            }
-        }
-        const uint8_t *st = stages + s * kGranBytes;
-        const uint8_t *xg = xs + m.xoff;
-#pragma unroll
-        for (int u = 0; u < kGranBytes >> kUnitShift; ++u) {
-            const int o = (u << kUnitShift) + lane * 16;
-            const uint4 a0 = *reinterpret_cast<const uint4 *>(st + o);
-            const uint4 a1 = *reinterpret_cast<const uint4 *>(st + o + 512);
-            const uint4 x0 = *reinterpret_cast<const uint4 *>(xg + o);
-            const uint4 x1 = *reinterpret_cast<const uint4 *>(xg + o + 512);
-            Vec32 av;
-            av.v[0] = a0.x, av.v[1] = a0.y, av.v[2] = a0.z, av.v[3] = a0.w;
-            av.v[4] = a1.x, av.v[5] = a1.y, av.v[6] = a1.z, av.v[7] = a1.w;
-            acc.unit(av, x0, x1);
-        }
-        if (m.last & 1) {
-            float sum = acc.total();
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) {
-                const int64_t row = m.row;
-                if (SPLIT) {
-                    a.part[grp * a.rows_total + row] = sum;
-                    if (m.last & 2) a.part[(grp ^ 1) * a.rows_total + row] = 0.0f;
-                } else {
-                    const int64_t b = row / a.M, i = row - b * a.M;
-                    uint8_t *yp = a.y + (b * a.stride_y_elems + i) * eo;
-                    store_out<DT_OUT>(yp, sum);
-                    final_to_peers<DT_OUT, SH>(a, row, sum);
-                }
-            }
-            acc = Acc<DT_IN>();
-        }
-        __syncwarp();  // every lane is done with stage s before it is refilled
-        if (!prod.next<SPLIT>(a, grp, small_grp, nwarps, lane, xs, b0, stages + s * kGranBytes, bars + s, metas + s) &&
-            lane == 0)
-            metas[s].row = -1;
-        __syncwarp();
-    }
-    if (timed_out) atomicOr(a.ctl + 3, 1ull);
-    if (lane == 0) {
-        s_tma_count[warp] = c;  // the stage at c was never filled: the next slot starts there
-        __threadfence();
-    }
-    __syncthreads();
-    if (SPLIT) meet_and_combine<DT_OUT, SH>(a, grp, idx, r0, r1);
-}
-
-// Every warp's stage barriers, once per CTA, before the first copy.
-template <bool TMA> __device__ __forceinline__ void tma_init(const GemvArgs &a, uint8_t *smem) {
-    if (!TMA) return;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.ring_off + kTmaBarOff);
-    for (int k = threadIdx.x; k < kTmaWarps * kTmaStages; k += blockDim.x) mbar_init(bars + k);
-    for (int w = threadIdx.x; w < kTmaWarps; w += blockDim.x) s_tma_count[w] = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    __syncthreads();
 }
 
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
@@ -820,6 +659,252 @@ template <int DT_OUT, bool SH> __device__ __forceinline__ void shard_gather(cons
     }
 }
 
+// Bounded wait for phase `parity` of a stage barrier (1 s); false when it ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t deadline = dev::globaltimer_ns() + 1000000000ull;
+    while (!mbar_try_wait(bar, parity))
+        if (dev::globaltimer_ns() > deadline) return false;
+    return true;
+}
+
+// Row pools of a ring call (batch 1).  The split pool, rows [0, whole_lo), is walked once by each
+// domain group: a group takes a row's granules homed in its domain and exchanges its partial with
+// the other group's (a row whose granules all sit in one domain is whole for that group and
+// skipped by the other).  The whole pool, rows [whole_lo, rows_total), is shared by both groups:
+// whoever claims a row takes all of it.  Rows are claimed pool_chunk at a time from one counter
+// per pool, so a domain group's SMs finish together whatever bandwidth each one gets, and the group
+// that drains its split pool first takes more of the whole rows.
+constexpr int kCtlEpoch = 0, kCtlDone = 1, kCtlFallback = 2, kCtlError = 3;
+constexpr int kCtlPool = 16;  // ctl[kCtlPool + 16 g]: next chunk of group g's split pool; g = 2: whole pool
+constexpr int kCtlWords = 64;
+
+__device__ __forceinline__ unsigned long long *pool_counter(const GemvArgs &a, int pool, int grp) {
+    return a.ctl + kCtlPool + 16 * (pool ? 2 : grp);
+}
+
+// A call's tag for the exchanged partials: never 0, which marks an empty exchange word.
+__device__ __forceinline__ uint32_t call_tag(unsigned long long epoch) {
+    return static_cast<uint32_t>(epoch % 0xffffffffull) + 1u;
+}
+
+// The warp's walk over its claimed rows, one granule at a time.  All 32 lanes run it in step: when
+// a row starts, lane l evaluates granule l's domain and one ballot gives the row's granules in this
+// group's domain (rows hold at most 32 granules: x fits in shared memory); each further granule is
+// the next bit of that mask.  Lane 0 claims chunks, records the stage's meta and starts its copy.
+template <bool SPLIT> struct PoolWalker {
+    int64_t row, end;       // rows of the current chunk still to walk: [row, end)
+    long long k2;           // a chunk of the CTA's first claim not yet started (-1: none)
+    unsigned long long nxt; // lane 0: the claim in flight for the chunk after this one
+    bool nxt_valid;
+    int pool;               // 0: this group's split rows, 1: whole rows, 2: nothing left
+    int grp, G;
+    uint32_t mask;          // granules of the current row still to fetch
+    bool whole;
+    const uint8_t *rowp;
+
+    __device__ __forceinline__ void start(const GemvArgs &a, int grp_, long long k_first, long long k_second) {
+        grp = grp_;
+        G = static_cast<int>(a.row_bytes >> kGranShift);
+        pool = SPLIT ? 0 : 1;
+        row = end = 0;
+        k2 = k_second;
+        nxt = static_cast<unsigned long long>(k_first);
+        nxt_valid = k_first >= 0;
+        mask = 0u;
+        whole = false;
+        rowp = nullptr;
+    }
+
+    // The next chunk: a chunk of the first claim, the claim in flight, or a new one; when a pool
+    // runs dry the walk moves to the whole pool.  The claim for the chunk after the one taken is
+    // issued at once, so its latency hides behind this chunk's copies.
+    __device__ __forceinline__ bool take_chunk(const GemvArgs &a, int lane) {
+        while (pool < 2) {
+            unsigned long long v = nxt;
+            if (!nxt_valid && lane == 0) v = atomicAdd(pool_counter(a, pool, grp), 1ull);
+            const long long k = static_cast<long long>(__shfl_sync(0xffffffffu, v, 0));
+            nxt_valid = false;
+            const int64_t lo = pool ? a.whole_lo : 0, hi = pool ? a.rows_total : a.whole_lo;
+            const int64_t r = lo + k * a.pool_chunk;
+            if (r < hi) {
+                row = r;
+                end = min(r + a.pool_chunk, hi);
+                if (k2 >= 0) {
+                    nxt = static_cast<unsigned long long>(k2);
+                    k2 = -1;
+                } else if (lane == 0) {
+                    nxt = atomicAdd(pool_counter(a, pool, grp), 1ull);
+                }
+                nxt_valid = true;
+                return true;
+            }
+            ++pool;
+            k2 = -1;
+        }
+        return false;
+    }
+
+    __device__ __forceinline__ bool next(const GemvArgs &a, int lane, uint8_t *stage, uint64_t *bar, TmaMeta *meta) {
+        while (mask == 0u) {
+            if (row >= end && !take_chunk(a, lane)) return false;
+            rowp = a.A + row * a.lda_bytes;
+            bool own = lane < G;
+            if (SPLIT && pool == 0 && own) {
+                const uint64_t u = (static_cast<uint64_t>(rowp - a.region_base) >> kUnitShift) +
+                                   (static_cast<uint64_t>(lane) << (kGranShift - kUnitShift));
+                own = unit_dom(a, u) == grp;
+            }
+            mask = __ballot_sync(0xffffffffu, own);
+            whole = !SPLIT || pool == 1 || mask == (G == 32 ? 0xffffffffu : (1u << G) - 1u);
+            if (mask == 0u) ++row;  // every granule is the other group's: the row is whole there
+        }
+        const int g = __ffs(mask) - 1;
+        mask &= mask - 1u;
+        if (lane == 0) {
+            meta->row = static_cast<int>(row);
+            meta->xoff = g * kGranBytes;
+            meta->last = (mask == 0u ? 1 : 0) | (whole ? 2 : 0);
+            mbar_expect_tx(bar, kGranBytes);
+            bulk_to_smem(stage, rowp + static_cast<int64_t>(g) * kGranBytes, kGranBytes, bar);
+        }
+        if (mask == 0u) ++row;
+        return true;
+    }
+};
+
+// Stages each warp has consumed so far in this launch: stage c % kTmaStages is used for the c-th
+// granule and its barrier completes phase c / kTmaStages, also across the walks of one CTA.
+__shared__ int s_tma_count[kTmaWarps];
+
+// Lane 0 of a warp, a split row's partial: one 64-bit exchange of (tag, partial) with the row's
+// word.  The word read back tells who was first: empty or stale (another call's tag), and this
+// warp was first -- the other group's warp will combine; this call's tag, and it holds the other
+// group's partial.  The second stores y = p0 + p1 (commutative, so both orders give the same
+// bits) and empties the word for the next call.  The exchange's result is only needed at the next
+// row end (or the walk's end), so the warp never waits for it.
+struct Pending {
+    int64_t row = -1;
+    float sum = 0.f;
+    unsigned long long old = 0ull;
+};
+
+template <int DT_OUT, bool SH> __device__ __forceinline__ void resolve(const GemvArgs &a, Pending &p, uint32_t tag) {
+    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    if (p.row < 0) return;
+    if (static_cast<uint32_t>(p.old >> 32) == tag) {
+        const float v = p.sum + __uint_as_float(static_cast<uint32_t>(p.old));
+        store_out<DT_OUT>(a.y + p.row * eo, v);
+        final_to_peers<DT_OUT, SH>(a, p.row, v);
+        a.xch[p.row] = 0ull;
+    }
+    p.row = -1;
+}
+
+// One warp's walk over the pools of group grp.  k_first / k_second: the warp's chunks of the CTA's
+// first claim (-1: claim from the start).  Before the first granule is consumed, x is staged
+// (stage_x_issue started its copies; SH: the flagged words), so the first copies of A overlap it.
+template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
+__device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long k_first, long long k_second,
+                                           uint32_t tag, int warp, int lane, uint8_t *smem, bool stage_x_now) {
+    constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
+    uint8_t *ring = smem + a.ring_off;
+    uint8_t *stages = ring + static_cast<size_t>(warp) * kTmaStages * kGranBytes;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ring + kTmaBarOff) + warp * kTmaStages;
+    TmaMeta *metas = reinterpret_cast<TmaMeta *>(ring + kTmaMetaOff) + warp * kTmaStages;
+    const uint8_t *xs = smem;
+
+    const int c0 = s_tma_count[warp];
+    PoolWalker<SPLIT> w;
+    w.start(a, grp, k_first, k_second);
+    for (int k = 0; k < kTmaStages; ++k) {
+        const int s = (c0 + k) % kTmaStages;
+        if (!w.next(a, lane, stages + s * kGranBytes, bars + s, metas + s) && lane == 0) metas[s].row = -1;
+    }
+    __syncwarp();
+    if (stage_x_now) {
+        if (SH) {
+            shard_stage_x<SH>(a, smem);
+        } else {
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            __syncthreads();
+        }
+    }
+
+    Acc<DT_IN> acc;
+    Pending pend;
+    bool timed_out = false;
+    int c = c0;
+    for (;; ++c) {
+        const int s = c % kTmaStages;
+        const TmaMeta m = metas[s];
+        if (m.row < 0) break;
+        if (!mbar_wait_bounded(bars + s, static_cast<uint32_t>(c / kTmaStages) & 1u)) {
+            timed_out = true;
+            break;
+        }
+        const uint8_t *st = stages + s * kGranBytes;
+        const uint8_t *xg = xs + m.xoff;
+#pragma unroll
+        for (int u = 0; u < kGranBytes >> kUnitShift; ++u) {
+            const int o = (u << kUnitShift) + lane * 16;
+            const uint4 a0 = *reinterpret_cast<const uint4 *>(st + o);
+            const uint4 a1 = *reinterpret_cast<const uint4 *>(st + o + 512);
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(xg + o);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(xg + o + 512);
+            Vec32 av;
+            av.v[0] = a0.x, av.v[1] = a0.y, av.v[2] = a0.z, av.v[3] = a0.w;
+            av.v[4] = a1.x, av.v[5] = a1.y, av.v[6] = a1.z, av.v[7] = a1.w;
+            acc.unit(av, x0, x1);
+        }
+        if (m.last & 1) {
+            float sum = acc.total();
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) {
+                const int64_t row = m.row;
+                if (!SPLIT || (m.last & 2)) {
+                    store_out<DT_OUT>(a.y + row * eo, sum);
+                    final_to_peers<DT_OUT, SH>(a, row, sum);
+                } else {
+                    resolve<DT_OUT, SH>(a, pend, tag);
+                    pend.old = atomicExch(a.xch + row, (static_cast<unsigned long long>(tag) << 32) |
+                                                           __float_as_uint(sum));
+                    pend.row = row;
+                    pend.sum = sum;
+                }
+            }
+            acc = Acc<DT_IN>();
+        }
+        __syncwarp();  // every lane is done with stage s before it is refilled
+        if (!w.next(a, lane, stages + s * kGranBytes, bars + s, metas + s) && lane == 0) metas[s].row = -1;
+        __syncwarp();
+    }
+    if (lane == 0) resolve<DT_OUT, SH>(a, pend, tag);
+    if (timed_out) {
+        // Copies still in flight land in this warp's stages: wait for them (bounded) before the CTA
+        // may exit; the call's results are void (error bit) and the walk stops here.
+        for (int k = 0; k < kTmaStages; ++k) {
+            const int s = (c + k) % kTmaStages;
+            if (metas[s].row >= 0) mbar_wait_bounded(bars + s, static_cast<uint32_t>((c + k) / kTmaStages) & 1u);
+        }
+        if (lane == 0) atomicOr(a.ctl + kCtlError, 1ull);
+    }
+    if (lane == 0) s_tma_count[warp] = c;  // the stage at c was never filled: the next walk starts there
+    __syncwarp();
+    return !timed_out;
+}
+
+// Shared-memory x of a batch-1 call: start every 16-byte copy (cp.async, no registers held); the
+// caller waits with cp.async.wait_all and a barrier once its first A copies are in flight.
+__device__ __forceinline__ void stage_x_issue(const GemvArgs &a, uint8_t *smem) {
+    const int64_t full16 = a.row_bytes / 16;
+    for (int64_t k = threadIdx.x; k < full16; k += blockDim.x) {
+        const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem + 16 * k));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(a.x + 16 * k) : "memory");
+    }
+}
+
 __device__ __forceinline__ unsigned long long ld_claim(const unsigned long long *p) {
     return *reinterpret_cast<const volatile unsigned long long *>(p);
 }
@@ -842,9 +927,70 @@ __device__ __forceinline__ int warp_claim_any(const GemvArgs &a, unsigned long l
     return -1;
 }
 
+// A ring call, the whole CTA.  Thread 0 claims up to 2 chunks per warp of its group's first pool in
+// one atomic (one claim per CTA at the start, not one per warp), x's copies start, the stage barriers
+// are initialised; then every warp walks the pools.  The done count carries each CTA's group in its
+// high half, so the last CTA knows whether a group had no CTA at all (its SMs were busy or absent)
+// and walks that group's split rows itself; it then resets the pool counters for the next call.
+// No CTA reads another's results, so nothing here needs a fence.
+template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
+__device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
+    __shared__ long long s_k0;
+    __shared__ unsigned long long s_done;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const uint32_t sm = dev::smid();
+    const int grp =
+        SPLIT && sm < static_cast<uint32_t>(kMaxSmid) ? static_cast<int>((a.grp_bits[sm >> 5] >> (sm & 31)) & 1u) : 0;
+    const unsigned long long epoch = ld_claim(a.ctl + kCtlEpoch) + 1ull;
+    const int first = a.first_chunks[grp];
+    if (tid == 0 && first > 0)
+        s_k0 = static_cast<long long>(atomicAdd(pool_counter(a, SPLIT ? 0 : 1, grp), static_cast<unsigned long long>(first)));
+    if (!SH) stage_x_issue(a, smem);
+    // The attr words reach L1 while the first claim is in flight: the first ballot of every warp
+    // reads them before its first copy can start.
+    if (SPLIT && a.dom_kind == 0 && tid < (a.attr_words + 31) / 32)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a.attr_bits + 32 * tid));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + a.ring_off + kTmaBarOff);
+    for (int k = tid; k < kTmaWarps * kTmaStages; k += blockDim.x) mbar_init(bars + k);
+    if (tid < kTmaWarps) s_tma_count[tid] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    const uint32_t tag = call_tag(epoch);
+    const long long k0 = s_k0;
+    walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, grp, warp < first ? k0 + warp : -1,
+                                         nwarps + warp < first ? k0 + nwarps + warp : -1, tag, warp, lane, smem, true);
+    __syncthreads();
+    if (tid == 0) s_done = atomicAdd(a.ctl + kCtlDone, 1ull | (static_cast<unsigned long long>(grp) << 32));
+    __syncthreads();
+    const unsigned long long before = s_done;
+    const bool last = static_cast<uint32_t>(before) + 1u == gridDim.x;
+    if (SPLIT && last) {
+        const uint32_t g1 = static_cast<uint32_t>(before >> 32) + static_cast<uint32_t>(grp);
+        const uint32_t g0 = gridDim.x - g1;
+        for (int g = 0; g < 2; ++g) {
+            if ((g ? g1 : g0) != 0u) continue;
+            if (tid == 0) atomicAdd(a.ctl + kCtlFallback, 1ull);
+            walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, g, -1, -1, tag, warp, lane, smem, false);
+            __syncthreads();
+        }
+    }
+    shard_gather<DT_OUT, SH>(a);
+    if (last && tid == 0) {
+        a.ctl[kCtlPool] = 0ull;
+        a.ctl[kCtlPool + 16] = 0ull;
+        a.ctl[kCtlPool + 32] = 0ull;
+        a.ctl[kCtlDone] = 0ull;
+        *reinterpret_cast<volatile unsigned long long *>(a.ctl + kCtlEpoch) = epoch;
+    }
+}
+
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH, bool TMA>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
+    if constexpr (TMA) {
+        ring_call<DT_IN, DT_OUT, SPLIT, SH>(a, smem);
+        return;
+    }
     __shared__ int s_slot;
     __shared__ int s_last;
     __shared__ int s_count;
@@ -872,15 +1018,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         if (lane < kMaxSmid / 32) s_left[lane] = 0u;
     }
     __syncthreads();
-    tma_init<TMA>(a, smem);
     shard_stage_x<SH>(a, smem);
-    if (s_slot >= 0) {
-        if (TMA) {
-            run_slot_tma<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
-        } else {
-            run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
-        }
-    }
+    if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -907,11 +1046,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     for (int w = 0; n_left && w < kMaxSmid / 32; ++w) {
         for (uint32_t m = s_left[w]; m; m &= m - 1u) {
             const int t = w * 32 + __ffs(m) - 1;
-            if (TMA) {
-                run_slot_tma<DT_IN, DT_OUT, SPLIT, SH>(a, t, warp, nwarps, lane, smem);
-            } else {
-                run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, t, warp, nwarps, lane, smem);
-            }
+            run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, t, warp, nwarps, lane, smem);
             __syncthreads();
         }
     }
@@ -1056,6 +1191,7 @@ struct l2d_plan {
     int32_t *d_sm_slot = nullptr;
     uint32_t *d_attr_bits = nullptr;
     float *d_part = nullptr;
+    unsigned long long *d_xch = nullptr;   // ring kernels' per-row exchange words
     unsigned int *d_meet = nullptr;
     size_t x_smem_bytes = 0;  // dynamic shared memory holding the x vectors (0 = read x through L1)
     bool tma = false;         // granule-ring kernels are available (TMA bulk copies of A)
@@ -1233,13 +1369,15 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
     const size_t o_attr = off;
     off = align256(off + n_attr_words * sizeof(uint32_t));
     const size_t o_ctl = off;
-    off = align256(off + 4 * sizeof(unsigned long long));
+    off = align256(off + kCtlWords * sizeof(unsigned long long));
     const size_t o_claim = off;
     off = align256(off + static_cast<size_t>(p->n_slots) * sizeof(unsigned long long));
     const size_t o_meet = off;
     off = align256(off + static_cast<size_t>(p->n_slots) * sizeof(unsigned int));
     const size_t o_part = off;
     off = align256(off + 2 * R * sizeof(float));
+    const size_t o_xch = off;
+    off = align256(off + R * sizeof(unsigned long long));
     p->dev_bytes = off;
     cudaError_t e = cudaMalloc(&p->dev_block, off);
     if (e != cudaSuccess) {
@@ -1253,6 +1391,7 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
     p->d_claim = reinterpret_cast<unsigned long long *>(blk + o_claim);
     p->d_meet = reinterpret_cast<unsigned int *>(blk + o_meet);
     p->d_part = reinterpret_cast<float *>(blk + o_part);
+    p->d_xch = reinterpret_cast<unsigned long long *>(blk + o_xch);
     e = cudaMemset(p->dev_block, 0, off);
     if (e == cudaSuccess) e = cudaMemcpy(p->d_sm_slot, slot.data(), kMaxSmid * sizeof(int32_t), cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
@@ -1273,11 +1412,11 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         const int64_t rb16 = (d.N * eb + 15) & ~int64_t(15);
         if (max_nb * rb16 <= kXSmemMax) p->x_smem_bytes = static_cast<size_t>(max_nb * rb16);
     }
-    // Granule-ring kernels: every row must start on a 4 KiB granule, x must sit in shared memory next
-    // to the rings, and the domain model must not split a granule.
-    if (!(d.flags & L2D_PLAN_NO_TMA) && p->x_smem_bytes > 0 && !(reinterpret_cast<uintptr_t>(d.A) & (kGranBytes - 1)) &&
-        (d.N * eb) % kGranBytes == 0 && (d.lda * eb) % kGranBytes == 0 &&
-        (d.batch == 1 || (d.stride_a * eb) % kGranBytes == 0) && (!p->has_domains || p->gran_shift >= kGranShift)) {
+    // Granule-ring kernels: one problem (batch 1), every row starting on a 4 KiB granule, x in shared
+    // memory next to the rings, and a domain model that does not split a granule.
+    if (!(d.flags & L2D_PLAN_NO_TMA) && d.batch == 1 && p->x_smem_bytes > 0 &&
+        !(reinterpret_cast<uintptr_t>(d.A) & (kGranBytes - 1)) && (d.N * eb) % kGranBytes == 0 &&
+        (d.lda * eb) % kGranBytes == 0 && (!p->has_domains || p->gran_shift >= kGranShift)) {
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device);
         const size_t ring_off = (p->x_smem_bytes + 1023) & ~size_t(1023);
@@ -1316,14 +1455,66 @@ int l2d_plan_destroy(l2d_plan *p) {
 
 namespace l2d {
 
-// Kernel choice, measured on B200: the rings win wherever the register pipeline's drain between row
-// visits shows (split calls up to ~2 GiB of A, or with rows of <= 16 KiB; unsplit calls below
-// 1 GiB); on larger, HBM-saturating calls the register kernels keep a 1-4 % edge.
+// Kernel choice, measured on B200: with row pools the granule-ring kernels are as fast as or faster
+// than the register kernels at every size measured, from the L2-resident 32 MiB case to 4 GiB
+// (AWARE 582 us against 630 us there), so every call the rings can take runs them.
 bool use_ring(const l2d_plan *p, bool split) {
-    if (!p->tma) return false;
-    if (p->tma_force) return true;
-    const int64_t row_bytes = p->desc.N * p->eb_in, a_bytes = p->rows_total * row_bytes;
-    return split ? (a_bytes < (int64_t(2) << 30) || row_bytes <= 16 * 1024) : a_bytes < (int64_t(1) << 30);
+    (void)split;
+    return p->tma;
+}
+
+// Pools of a ring call.
+//  * Rows are claimed in chunks of about 32 KiB of A, smaller when the call has fewer than 4 chunks
+//    per warp of the grid.  Each CTA's first claim takes up to 2 chunks per warp in one atomic, and
+//    at most a quarter of its even share of the pool, so a small pool is not swallowed by the first
+//    CTAs to start.
+//  * Unsplit calls have only whole rows.  The swapped control keeps every row split (no near reads
+//    at all).  AWARE and OBLIVIOUS calls put the last rows in the whole pool: the bytes the faster
+//    domain group can stream while the slower one finishes its split rows -- group g's split work
+//    per SM is the bytes homed in its domain (half of A for OBLIVIOUS) over its SM count -- plus
+//    L2D_WHOLE_EXTRA_PERMILLE of A as the margin either group draws on when its SMs get less
+//    bandwidth.
+#ifndef L2D_WHOLE_EXTRA_PERMILLE
+#define L2D_WHOLE_EXTRA_PERMILLE 10
+#endif
+struct RingPools {
+    int64_t whole_lo = 0;  // rows [whole_lo, rows_total) are the whole pool
+    int64_t chunk = 1;     // rows per claim
+    int first[2] = {0, 0}; // chunks of each group's CTAs' first claim (group 0's for unsplit calls)
+};
+
+RingPools ring_pools(const l2d_plan *p, bool split, int mode) {
+    RingPools rp;
+    const int64_t R = p->rows_total, rb = std::max<int64_t>(p->desc.N * p->eb_in, 1);
+    const int64_t warps = static_cast<int64_t>(std::max(p->n_slots, 1)) * kTmaWarps;
+    rp.chunk = std::max<int64_t>(1, std::min<int64_t>({16, (int64_t(32) << 10) / rb, R / (4 * warps)}));
+    int n_ctas[2] = {p->n_slots, p->n_slots};
+    if (!split) {
+        rp.whole_lo = 0;
+    } else {
+        n_ctas[0] = std::max(p->n_dom[0], 1);
+        n_ctas[1] = std::max(p->n_dom[1], 1);
+        if (mode == L2D_MODE_SWAPPED) {
+            rp.whole_lo = R;
+        } else {
+            const double total = static_cast<double>(R) * rb;
+            double D[2] = {total / 2, total / 2};
+            if (mode == L2D_MODE_AWARE && p->domain_bytes[0] + p->domain_bytes[1] > 0) {
+                D[0] = static_cast<double>(p->domain_bytes[0]);
+                D[1] = static_cast<double>(p->domain_bytes[1]);
+            }
+            const double t0 = D[0] / n_ctas[0], t1 = D[1] / n_ctas[1];
+            const double lag = t0 > t1 ? (t0 - t1) * n_ctas[1] : (t1 - t0) * n_ctas[0];
+            const double whole_bytes = lag + total * L2D_WHOLE_EXTRA_PERMILLE / 1000.0;
+            const int64_t whole = std::min<int64_t>(R, static_cast<int64_t>(std::ceil(whole_bytes / rb)));
+            rp.whole_lo = R - whole;
+        }
+    }
+    const int64_t pool_rows = split ? rp.whole_lo : R;
+    const int64_t chunks = (pool_rows + rp.chunk - 1) / rp.chunk;
+    for (int g = 0; g < 2; ++g)
+        rp.first[g] = static_cast<int>(std::min<int64_t>(2 * kTmaWarps, chunks / (4 * int64_t(n_ctas[g]))));
+    return rp;
 }
 
 // Kernel arguments of one call on plan p (no sharding); *split tells which kernel variant runs.
@@ -1352,6 +1543,7 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.rows_total = p->rows_total;
     a.region_base = split ? p->region_base : p->stream_base;
     a.attr_bits = p->d_attr_bits;
+    a.attr_words = static_cast<int64_t>((p->attr.size() + 31) / 32);
     a.mask = p->mask;
     a.gran_shift = p->gran_shift;
     a.dom_kind = mode == L2D_MODE_OBLIVIOUS ? 1 : 0;
@@ -1367,6 +1559,15 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.x_smem = p->x_smem_bytes > 0;
     a.ring_off = static_cast<int>(p->ring_off);
     a.use_tma = use_ring(p, split) ? 1 : 0;
+    a.xch = p->d_xch;
+    const RingPools rp = ring_pools(p, split, mode);
+    a.whole_lo = rp.whole_lo;
+    a.pool_chunk = rp.chunk;
+    a.first_chunks[0] = rp.first[0];
+    a.first_chunks[1] = rp.first[1];
+    if (p->has_domains)
+        for (int s = 0; s < p->num_sm && s < kMaxSmid; ++s)
+            if (p->sm_domain[s] & 1) a.grp_bits[s >> 5] |= 1u << (s & 31);
     // Balance between unequal domain groups: with n_small < n_big SMs, the bigger group also takes a
     // fraction (n_big - n_small)/(n_big + n_small) of the rows whole, spread evenly, so every SM
     // streams the same bytes.  The swapped control stays pure (no spill rows).
@@ -1386,6 +1587,7 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
 // (a call that reaches the kernel with a missing scratch pointer is refused, never launched).
 int check_args(const GemvArgs &a) {
     if (!a.x || !a.y || !a.sm_slot || !a.part || !a.meet || !a.claim || !a.ctl || a.n_slots <= 0 ||
+        (a.use_tma && (!a.xch || a.pool_chunk <= 0 || a.whole_lo < 0 || a.whole_lo > a.rows_total || !a.x_smem)) ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
     if (a.shard_world > 1 && (!a.peer_xw || !a.peer_yw || !a.shard_status || !a.x_smem || a.rows_total != a.M ||
@@ -1469,6 +1671,11 @@ int l2d_plan_stats_get(l2d_plan *p, l2d_plan_stats *s) {
     s->ring_modes = 0;
     for (int m = L2D_MODE_OBLIVIOUS; m <= L2D_MODE_STREAM; ++m)
         if (use_ring(p, m != L2D_MODE_STREAM && p->desc.N > 0)) s->ring_modes |= 1 << m;
+    if (p->tma) {
+        const RingPools rp = ring_pools(p, p->has_domains && p->desc.N > 0, L2D_MODE_AWARE);
+        s->ring_chunk_rows = rp.chunk;
+        s->ring_whole_rows = p->rows_total - rp.whole_lo;
+    }
     s->scratch_bytes = p->dev_bytes;
     int prev = -1;
     cudaGetDevice(&prev);
@@ -1518,7 +1725,7 @@ namespace l2d {
 namespace noalloc {
 
 constexpr size_t kCtlOff = 0;
-constexpr size_t kClaimOff = 256;
+constexpr size_t kClaimOff = kCtlWords * sizeof(unsigned long long);
 constexpr size_t kMeetOff = kClaimOff + kMaxSmid * sizeof(unsigned long long);
 constexpr size_t kSlotOff = kMeetOff + kMaxSmid * sizeof(unsigned int);
 constexpr size_t kAttrOff = kSlotOff + kMaxSmid * sizeof(int32_t);

@@ -67,13 +67,13 @@ def oracle_y(A, x, dtype, M, N, lda, batch, dtype_out):
     return np.concatenate(ys)
 
 
-def run_gemv(A_h, x_h, M, N, dtype, dtype_out, modes, lda=None, batch=1):
+def run_gemv(A_h, x_h, M, N, dtype, dtype_out, modes, lda=None, batch=1, tma=None):
     lda = lda or N
     eb = L.ELEM_BYTES[dtype]
     raw, A = aligned_empty(max(A_h.nbytes, 16))
     A[: A_h.nbytes].copy_(to_dev(A_h).view(torch.uint8).reshape(-1)) if A_h.nbytes else None
     x = to_dev(x_h) if x_h.size else torch.zeros(8, dtype=torch.float32, device="cuda")
-    plan = L.GemvPlan(A, M, N, dtype, dtype_out, lda=lda, batch=batch)
+    plan = L.GemvPlan(A, M, N, dtype, dtype_out, lda=lda, batch=batch, tma=tma)
     outs = {}
     for mode in modes:
         if dtype_out == L.F32:
@@ -165,16 +165,16 @@ def test_aware_and_swapped_bit_identical_and_deterministic(dev):
     partials are the same sums, combined commutatively.  (AWARE also hands the bigger domain
     group an evenly spread fraction (n_big - n_small)/(n_big + n_small) of the rows whole, to
     balance unequal SM counts; SWAPPED does not, so those rows are left out.)  Repeated calls
-    are bit-identical."""
+    are bit-identical.  (The register kernels; the granule-ring kernels have their own test.)"""
     M, N = 1024, 8192
     A, x = host_inputs(M, N, L.F16)
-    outs, stats = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED])
+    outs, stats = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED], tma=False)
     n0, n1 = stats["domain_sms"]
     num, den = abs(n1 - n0), n0 + n1
     split_rows = np.array([num == 0 or (r + 1) * num // den == r * num // den for r in range(M)])
     assert split_rows.sum() > M // 2
     assert np.array_equal(outs[L.MODE_AWARE][split_rows], outs[L.MODE_SWAPPED][split_rows])
-    outs2, _ = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE])
+    outs2, _ = run_gemv(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE], tma=False)
     assert np.array_equal(outs[L.MODE_AWARE], outs2[L.MODE_AWARE])
     assert stats["calls"] == 2 and n0 > 0 and n1 > 0
 

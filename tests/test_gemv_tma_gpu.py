@@ -2,8 +2,12 @@
 
 Same bars as the register kernels: fp32 relative L2 <= 1e-5 and fp16/bf16 <= 2e-3 against the fp64
 oracle (of the same rounded inputs, rounded to the output type); the exact-integer inputs
-bit-exact; AWARE and SWAPPED bit-identical on split rows; repeated calls bit-identical.  A shape
-the ring kernels cannot take (rows off the 4 KiB granules) falls back to the register kernels.
+bit-exact.  The ring kernels claim rows from pools, so the tests also pin what must not depend on
+who claimed what: AWARE and SWAPPED bit-identical on every split-pool row (the same two partials,
+added commutatively), rows taken whole bit-identical with STREAM (one warp, granules in order),
+repeated calls bit-identical whatever ran in between (the exchange words empty themselves, the pool
+counters reset).  Shapes the ring kernels cannot take (rows off the 4 KiB granules, batched
+problems) run the register kernels.
 """
 import json
 import os
@@ -81,8 +85,8 @@ def oracle(A, x, dtype, M, N, batch, dtype_out):
     (2049, 8192, L.BF16, L.BF16, 1),   # 16 KiB rows
     (1500, 2048, L.F32, L.F32, 1),     # 8 KiB fp32 rows
     (513, 16384, L.F16, L.F32, 1),     # 32 KiB rows, fp32 out
-    (300, 4096, L.F16, L.F16, 3),      # batched, granule-aligned problem stride
     (7, 2048, L.BF16, L.F32, 1),       # fewer rows than warps
+    (20000, 1024, L.F32, L.F32, 1),    # 4 KiB rows: one granule, so every row is whole for one group
 ])
 def test_ring_kernels_match_oracle(dev, M, N, dtype, dtype_out, batch):
     A, x = inputs(M, N, dtype, batch)
@@ -108,13 +112,43 @@ def test_ring_kernels_integer_kat_bit_exact(dev):
 def test_ring_kernels_aware_swapped_identical_and_deterministic(dev):
     M, N = 1024, 8192
     A, x = inputs(M, N, L.F16)
-    outs, stats = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_AWARE])
-    n0, n1 = stats["domain_sms"]
-    num, den = abs(n1 - n0), n0 + n1
-    split_rows = np.array([num == 0 or (r + 1) * num // den == r * num // den for r in range(M)])
-    assert np.array_equal(outs[L.MODE_AWARE][split_rows], outs[L.MODE_SWAPPED][split_rows])
+    outs, stats = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_STREAM])
+    whole = stats["ring_whole_rows"]
+    assert 0 < whole < M // 4 and stats["ring_chunk_rows"] >= 1
+    pool = M - whole
+    assert np.array_equal(outs[L.MODE_AWARE][:pool], outs[L.MODE_SWAPPED][:pool])
+    # Whole rows (one warp, every granule in order) are STREAM's arithmetic exactly.
+    assert np.array_equal(outs[L.MODE_AWARE][pool:], outs[L.MODE_STREAM][pool:])
     outs2, _ = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE])
     assert np.array_equal(outs[L.MODE_AWARE], outs2[L.MODE_AWARE])
+
+
+def test_ring_calls_repeat_bit_identical_across_modes(dev):
+    """Six calls on one plan, modes interleaved: every AWARE call gives the same bits, so each call
+    leaves the exchange words empty and the pool counters at zero for the next."""
+    M, N = 3000, 4096
+    A_h, x_h = inputs(M, N, L.BF16)
+    nbytes = A_h.nbytes
+    raw = torch.empty(nbytes + PAGE, dtype=torch.uint8, device="cuda")
+    off = (-raw.data_ptr()) % PAGE
+    A = raw[off: off + nbytes]
+    A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
+    x = to_dev(x_h)
+    plan = L.GemvPlan(A, M, N, L.BF16, L.F32, tma=True)
+    ys = []
+    for mode in [L.MODE_AWARE, L.MODE_OBLIVIOUS, L.MODE_AWARE, L.MODE_STREAM, L.MODE_SWAPPED, L.MODE_AWARE]:
+        y = torch.full((M,), float("nan"), dtype=torch.float32, device="cuda")
+        plan.gemv(A, x, y, mode)
+        if mode == L.MODE_AWARE:
+            ys.append(y)
+    torch.cuda.synchronize()
+    stats = plan.stats()
+    plan.close()
+    assert stats["calls"] == 6 and stats["device_errors"] == 0 and stats["fallback_slots"] == 0
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+    ref = oracle(A_h, x_h, L.BF16, M, N, 1, L.F32)
+    assert O.rel_l2(ref.astype(np.float64), ys[0].cpu().numpy()) <= TOL[L.BF16]
 
 
 def test_ring_kernels_agree_with_register_kernels(dev):
@@ -125,6 +159,16 @@ def test_ring_kernels_agree_with_register_kernels(dev):
     assert s1["tma"] == 2 and s0["tma"] == 0
     a, b = ring[L.MODE_AWARE].astype(np.float64), reg[L.MODE_AWARE].astype(np.float64)
     assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-5
+
+
+def test_batched_problems_run_register_kernels(dev):
+    M, N, batch = 300, 4096, 3  # granule-aligned rows and problem stride, but three problems
+    A, x = inputs(M, N, L.F16, batch)
+    outs, stats = run(A, x, M, N, L.F16, L.F16, ALL_MODES, batch)
+    assert stats["tma"] == 0
+    ref = oracle(A, x, L.F16, M, N, batch, L.F16)
+    for m in ALL_MODES:
+        assert O.rel_l2(ref.astype(np.float64), outs[m]) <= TOL[L.F16]
 
 
 def test_unaligned_rows_fall_back_to_register_kernels(dev):
