@@ -717,8 +717,7 @@ template <bool SPLIT> struct PoolWalker {
     }
 
     // The next chunk: a chunk of the first claim, the claim in flight, or a new one; when a pool
-    // runs dry the walk moves to the whole pool.  The claim for the chunk after the one taken is
-    // issued at once, so its latency hides behind this chunk's copies.
+    // runs dry the walk moves to the whole pool.
     __device__ __forceinline__ bool take_chunk(const GemvArgs &a, int lane) {
         while (pool < 2) {
             unsigned long long v = nxt;
@@ -732,17 +731,24 @@ template <bool SPLIT> struct PoolWalker {
                 end = min(r + a.pool_chunk, hi);
                 if (k2 >= 0) {
                     nxt = static_cast<unsigned long long>(k2);
+                    nxt_valid = true;
                     k2 = -1;
-                } else if (lane == 0) {
-                    nxt = atomicAdd(pool_counter(a, pool, grp), 1ull);
                 }
-                nxt_valid = true;
                 return true;
             }
             ++pool;
             k2 = -1;
         }
         return false;
+    }
+
+    // The claim for the next chunk goes out with the copy of this chunk's last granule: its latency
+    // hides behind the granules still in the ring, and a warp never holds a chunk it will not start
+    // for long -- when a pool runs dry, every warp has at most the rest of one chunk left.
+    __device__ __forceinline__ void claim_ahead(const GemvArgs &a, int lane) {
+        if (nxt_valid || pool >= 2 || mask != 0u || row + 1 < end) return;
+        if (lane == 0) nxt = atomicAdd(pool_counter(a, pool, grp), 1ull);
+        nxt_valid = true;
     }
 
     __device__ __forceinline__ bool next(const GemvArgs &a, int lane, uint8_t *stage, uint64_t *bar, TmaMeta *meta) {
@@ -768,6 +774,7 @@ template <bool SPLIT> struct PoolWalker {
             mbar_expect_tx(bar, kGranBytes);
             bulk_to_smem(stage, rowp + static_cast<int64_t>(g) * kGranBytes, kGranBytes, bar);
         }
+        claim_ahead(a, lane);
         if (mask == 0u) ++row;
         return true;
     }
