@@ -49,6 +49,9 @@ constexpr int kUnitShift = 10;  // 1 KiB units: 32 bytes per lane
 constexpr int kThreads = 512;
 constexpr int kUnroll = 8;      // units in flight per warp
 constexpr int kXSmemMax = 96 * 1024;
+#ifndef L2D_PDL
+#define L2D_PDL 1  // programmatic dependent launch of plan calls (0: plain stream order)
+#endif
 
 struct GemvArgs {
     const uint8_t *A;
@@ -967,6 +970,7 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
     walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, grp, warp < first ? k0 + warp : -1,
                                          nwarps + warp < first ? k0 + nwarps + warp : -1, tag, warp, lane, smem, true);
     __syncthreads();
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) s_done = atomicAdd(a.ctl + kCtlDone, 1ull | (static_cast<unsigned long long>(grp) << 32));
     __syncthreads();
     const unsigned long long before = s_done;
@@ -994,6 +998,9 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH, bool TMA>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
+    // A launch that overlaps the previous GEMV's tail (programmatic dependent launch) waits here
+    // for that grid to complete and its writes to be visible; otherwise this returns at once.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if constexpr (TMA) {
         ring_call<DT_IN, DT_OUT, SPLIT, SH>(a, smem);
         return;
@@ -1028,6 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     shard_stage_x<SH>(a, smem);
     if (s_slot >= 0) run_slot<DT_IN, DT_OUT, SPLIT, SH>(a, s_slot, warp, nwarps, lane, smem);
     __syncthreads();
+    if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
         __threadfence();
         const unsigned long long done = atomicAdd(a.ctl + 1, 1ull);
@@ -1610,12 +1618,23 @@ int launch_args(l2d_plan *p, const GemvArgs &a, bool split, void *stream) {
     int prev = -1;
     cudaGetDevice(&prev);
     if (prev != p->device) cudaSetDevice(p->device);
-    if (a.use_tma) {
-        k<<<p->n_slots, kTmaThreads, p->ring_off + kTmaBlockBytes, static_cast<cudaStream_t>(stream)>>>(a);
-    } else {
-        k<<<p->n_slots, kThreads, p->x_smem_bytes, static_cast<cudaStream_t>(stream)>>>(a);
-    }
-    cudaError_t e = cudaGetLastError();
+    // Programmatic dependent launch: when the previous kernel in the stream is a GEMV, each of its
+    // CTAs lets this launch take its SM once that CTA's rows are done, so the launch and the
+    // prologue overlap the previous call's tail.  The kernel waits for the previous grid
+    // (griddepcontrol.wait) before its first global access; after any other kernel this is an
+    // ordinary stream-ordered launch.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(p->n_slots));
+    cfg.blockDim = dim3(a.use_tma ? kTmaThreads : kThreads);
+    cfg.dynamicSmemBytes = a.use_tma ? p->ring_off + kTmaBlockBytes : p->x_smem_bytes;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = L2D_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, k, a);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (prev >= 0 && prev != p->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "gemv launch: %s", cudaGetErrorString(e));
     return L2D_OK;

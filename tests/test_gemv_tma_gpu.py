@@ -124,8 +124,9 @@ def test_ring_kernels_aware_swapped_identical_and_deterministic(dev):
 
 
 def test_ring_calls_repeat_bit_identical_across_modes(dev):
-    """Six calls on one plan, modes interleaved: every AWARE call gives the same bits, so each call
-    leaves the exchange words empty and the pool counters at zero for the next."""
+    """Six calls on one plan, modes interleaved, launched back to back (each launch may overlap the
+    previous call's tail): every AWARE call gives the same bits, so each call leaves the exchange
+    words empty and the pool counters at zero for the next, and no call reads state early."""
     M, N = 3000, 4096
     A_h, x_h = inputs(M, N, L.BF16)
     nbytes = A_h.nbytes
@@ -135,13 +136,13 @@ def test_ring_calls_repeat_bit_identical_across_modes(dev):
     A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
     x = to_dev(x_h)
     plan = L.GemvPlan(A, M, N, L.BF16, L.F32, tma=True)
-    ys = []
-    for mode in [L.MODE_AWARE, L.MODE_OBLIVIOUS, L.MODE_AWARE, L.MODE_STREAM, L.MODE_SWAPPED, L.MODE_AWARE]:
-        y = torch.full((M,), float("nan"), dtype=torch.float32, device="cuda")
-        plan.gemv(A, x, y, mode)
-        if mode == L.MODE_AWARE:
-            ys.append(y)
+    modes = [L.MODE_AWARE, L.MODE_OBLIVIOUS, L.MODE_AWARE, L.MODE_STREAM, L.MODE_SWAPPED, L.MODE_AWARE]
+    outs = [torch.full((M,), float("nan"), dtype=torch.float32, device="cuda") for _ in modes]
     torch.cuda.synchronize()
+    for mode, y in zip(modes, outs):
+        plan.gemv(A, x, y, mode)
+    torch.cuda.synchronize()
+    ys = [y for mode, y in zip(modes, outs) if mode == L.MODE_AWARE]
     stats = plan.stats()
     plan.close()
     assert stats["calls"] == 6 and stats["device_errors"] == 0 and stats["fallback_slots"] == 0
@@ -179,3 +180,35 @@ def test_unaligned_rows_fall_back_to_register_kernels(dev):
     ref = oracle(A, x, L.F16, M, N, 1, L.F16)
     for m in ALL_MODES:
         assert O.rel_l2(ref.astype(np.float64), outs[m]) <= TOL[L.F16]
+
+
+def test_back_to_back_calls_of_two_plans(dev):
+    """Calls of two plans alternate back to back on one stream, x of the second written by a copy
+    between them: every result matches its own plan's result from a lone call."""
+    shapes = [(2048, 8192, L.F16), (1024, 4096, L.BF16)]
+    plans, mats, xs, lone = [], [], [], []
+    for i, (M, N, dt) in enumerate(shapes):
+        A_h, x_h = inputs(M, N, dt)
+        raw = torch.empty(A_h.nbytes + PAGE, dtype=torch.uint8, device="cuda")
+        off = (-raw.data_ptr()) % PAGE
+        A = raw[off: off + A_h.nbytes]
+        A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
+        x = to_dev(x_h)
+        plan = L.GemvPlan(A, M, N, dt, L.F32)
+        y = torch.empty(M, dtype=torch.float32, device="cuda")
+        plan.gemv(A, x, y, L.MODE_AWARE)
+        torch.cuda.synchronize()
+        plans.append(plan); mats.append((raw, A)); xs.append(x); lone.append(y)
+    x2 = torch.empty_like(xs[1])
+    outs = [[torch.empty_like(lone[i]) for _ in range(4)] for i in range(2)]
+    torch.cuda.synchronize()
+    for k in range(4):
+        plans[0].gemv(mats[0][1], xs[0], outs[0][k], L.MODE_AWARE)
+        x2.copy_(xs[1])
+        plans[1].gemv(mats[1][1], x2, outs[1][k], L.MODE_AWARE)
+    torch.cuda.synchronize()
+    for i in range(2):
+        for k in range(4):
+            assert torch.equal(outs[i][k], lone[i]), f"plan {i} call {k}"
+        assert plans[i].stats()["device_errors"] == 0
+        plans[i].close()
