@@ -219,16 +219,19 @@ L2D_API int l2d_plan_stats_get(l2d_plan *plan, l2d_plan_stats *stats);
 L2D_API int l2d_plan_domain_map(const l2d_plan *plan, int *sm_domain, int cap, int *num_sm, uint32_t *mask);
 
 /* ---- allocation-free GEMV (no counterpart in the reference) ----
- * For callers that cannot allocate device memory when they run a GEMV: runtimes that reserve all
- * HBM for their own pools at start-up, code inside a CUDA stream capture, latency-critical paths
- * that must not enter the allocator.  Same kernel and modes as l2d_gemv, but no plan: the scratch
- * is a file-scope device array of the library (about 1.6 MiB per GPU, held until exit), so the
- * call allocates nothing.  The caller passes A (desc->A), x, y and, for every mode but STREAM,
- * the domain map (l2d_probe_sm_domains / l2d_probe_addr_domains output; map may be NULL for
- * STREAM).  The first call on a device looks up the array's address and clears it, synchronously;
- * make that first call before any stream capture.  Calls share the array: calls that overlap on
- * the GPU race and must be serialised by the caller.  Sizes beyond the limits below return
- * L2D_ERR_INVALID. */
+ * For callers that cannot allocate device memory when they run a GEMV: serving runtimes that
+ * reserve all HBM for their own pools at start-up and forbid later allocations, and latency-
+ * critical paths that must not enter the allocator (cudaMalloc can synchronise the device).  Same
+ * kernel and modes as l2d_gemv, but no plan: the scratch is a file-scope device array of the
+ * library (about 1.6 MiB per GPU, held until exit), so the call allocates nothing.  The caller
+ * passes A (desc->A), x, y and, for every mode but STREAM, the domain map (l2d_probe_sm_domains /
+ * l2d_probe_addr_domains output; map may be NULL for STREAM).  Each call launches a one-CTA
+ * set-up kernel that receives the call's SM->slot table and attr bits as kernel parameters, then
+ * the GEMV kernel; nothing is copied from host memory.  The first call on a device looks up the
+ * array's address and clears it, synchronously; make that first call before any stream capture.
+ * Calls share the array and each leaves its contents for the next: calls that overlap on the GPU
+ * (other streams, other threads) race and must be serialised by the caller.  Sizes beyond the
+ * limits below return L2D_ERR_INVALID. */
 #define L2D_NOALLOC_MAX_ROWS 196608  /* batch * M */
 #define L2D_NOALLOC_MAX_PAGES 32768  /* 2 MiB pages spanned by the domain map (64 GiB of A) */
 L2D_API int l2d_gemv_noalloc(const l2d_gemv_desc *desc, const l2d_domain_map *map, const void *x, void *y,

@@ -1734,17 +1734,17 @@ int l2d_plan_domain_map(const l2d_plan *p, int *sm_domain, int cap, int *num_sm,
 // Allocation-free entry point.
 //
 // Some callers cannot call cudaMalloc when they need a GEMV: a serving runtime that reserves nearly
-// all HBM for its own pools at start-up and forbids later allocations, code running between
-// cudaStreamBeginCapture and cudaStreamEndCapture (a cudaMalloc there breaks the capture), or a
-// latency-critical path that must not enter the allocator.  l2d_gemv_noalloc runs the same kernel
-// as l2d_gemv without a plan: its scratch (control words, slot claims, the SM->slot table, the
-// attr bits, the interval counters and two partials per row) lives in the file-scope array below,
-// which every GPU that loads this library holds until the process exits.  Limits:
-// L2D_NOALLOC_MAX_ROWS rows over all problems, L2D_NOALLOC_MAX_PAGES 2 MiB pages of A.  Every call
-// shares the array and leaves its contents for the next call (the interval counters return to zero
-// when a call completes), so calls
-// that overlap on the GPU (other streams, other threads) race and must be serialised by the
-// caller.
+// all HBM for its own pools at start-up and forbids later allocations, or a latency-critical path
+// that must not enter the allocator (cudaMalloc can synchronise the device).  l2d_gemv_noalloc
+// runs the same kernel as l2d_gemv without a plan: its scratch (control words, slot claims, the
+// SM->slot table, the attr bits, the interval counters and two partials per row) lives in the
+// file-scope array below, which every GPU that loads this library holds until the process exits.
+// Limits: L2D_NOALLOC_MAX_ROWS rows over all problems, L2D_NOALLOC_MAX_PAGES 2 MiB pages of A.
+// The per-call tables (SM->slot, attr bits) travel as kernel parameters of a one-CTA set-up kernel
+// that writes them into the array, so a call copies nothing from host memory.  Every call shares
+// the array and leaves its contents for the next call (the interval counters return to zero when
+// a call completes), so calls that overlap on the GPU (other streams, other threads) race and must
+// be serialised by the caller.
 // ---------------------------------------------------------------------------------------------
 
 namespace l2d {
@@ -1760,6 +1760,21 @@ constexpr size_t kBytes = kPartOff + 2 * static_cast<size_t>(L2D_NOALLOC_MAX_ROW
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_scratch[kBytes];
+
+// The call's SM->slot table and attr bits, passed by value (8 KiB of kernel parameters; the limit
+// is 32 KiB on sm_70 and later with CUDA 12.1+).
+struct Tables {
+    int32_t slot[kMaxSmid];
+    uint32_t attr_bits[L2D_NOALLOC_MAX_PAGES / 32];
+    uint32_t attr_words;
+};
+
+__global__ void k_noalloc_tables(const Tables t, uint8_t *scratch) {
+    int32_t *slot = reinterpret_cast<int32_t *>(scratch + kSlotOff);
+    uint32_t *attr = reinterpret_cast<uint32_t *>(scratch + kAttrOff);
+    for (int i = threadIdx.x; i < kMaxSmid; i += blockDim.x) slot[i] = t.slot[i];
+    for (uint32_t i = threadIdx.x; i < t.attr_words; i += blockDim.x) attr[i] = t.attr_bits[i];
+}
 
 std::mutex g_mu;
 uint8_t *g_ptr[kMaxDevices] = {nullptr};
@@ -1832,15 +1847,19 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
     } restore{prev, d.device};
     int num_sm = 0;
     L2D_CUDA_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, d.device));
+    if (num_sm > kMaxSmid)
+        return set_error(L2D_ERR_UNSUPPORTED, "gemv_noalloc: %d SMs exceed the slot table (%d)", num_sm, kMaxSmid);
     uint8_t *scratch = nullptr;
     int st = noalloc::setup(d.device, &scratch);
     if (st != L2D_OK) return st;
 
-    // Host tables on the stack: SM -> slot and the attr bits of the pages A's rows touch.
+    // The call's tables (SM -> slot and the attr bits of the pages A's rows touch), built here and
+    // handed to the set-up kernel by value.
     const uint64_t A = reinterpret_cast<uint64_t>(d.A);
     const uint64_t span = static_cast<uint64_t>(((R - 1) / d.M * d.stride_a + (R - 1) % d.M * d.lda + d.N) * eb);
-    int32_t slot[kMaxSmid];
-    uint32_t attr_bits[L2D_NOALLOC_MAX_PAGES / 32];
+    noalloc::Tables tab;
+    int32_t *slot = tab.slot;
+    uint32_t *attr_bits = tab.attr_bits;
     int n_dom[2] = {0, 0};
     size_t attr_words = 1;
     attr_bits[0] = 0;
@@ -1870,12 +1889,12 @@ extern "C" int l2d_gemv_noalloc(const l2d_gemv_desc *desc_in, const l2d_domain_m
         mask = map->mask;
         gran_shift = lowest_bit_or(mask, kPageShift);
     } else {
-        for (int s = 0; s < num_sm && s < kMaxSmid; ++s) slot[s] = s;
+        for (int s = 0; s < num_sm; ++s) slot[s] = s;
     }
+    tab.attr_words = static_cast<uint32_t>(attr_words);
     cudaStream_t cs = static_cast<cudaStream_t>(stream);
-    L2D_CUDA_TRY(cudaMemcpyAsync(scratch + noalloc::kSlotOff, slot, sizeof slot, cudaMemcpyHostToDevice, cs));
-    L2D_CUDA_TRY(cudaMemcpyAsync(scratch + noalloc::kAttrOff, attr_bits, attr_words * sizeof(uint32_t),
-                                 cudaMemcpyHostToDevice, cs));
+    noalloc::k_noalloc_tables<<<1, 256, 0, cs>>>(tab, scratch);
+    L2D_CUDA_TRY(cudaGetLastError());
 
     GemvArgs a;
     std::memset(&a, 0, sizeof a);

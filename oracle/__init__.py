@@ -49,6 +49,7 @@ def lib() -> C.CDLL:
         L.or_cfg_value.restype = C.c_float
         L.or_cfg_value.argtypes = [u64, u64, u64, C.c_int, C.c_float, C.c_float]
         L.or_cfg_fill.argtypes = [vp, u64, u64, u64, u64, C.c_int, C.c_float, C.c_float]
+        L.or_cfg_fill_mt.argtypes = [vp, u64, u64, u64, u64, C.c_int, C.c_float, C.c_float, C.c_int]
         L.or_f32_to_f16.restype = C.c_uint16
         L.or_f32_to_f16.argtypes = [C.c_float]
         L.or_f16_to_f32.restype = C.c_float
@@ -98,9 +99,15 @@ def ref_fill(n: int, seed: int, stream: int, integer_mode: bool = False, first: 
     return out
 
 
-def cfg_fill(n: int, seed: int, stream: int, dist: int, p0: float, p1: float, first: int = 0) -> np.ndarray:
+def cfg_fill(n: int, seed: int, stream: int, dist: int, p0: float, p1: float, first: int = 0,
+             threads: int = 1) -> np.ndarray:
+    """BASELINE-config values of flat indices [first, first + n) (counter-based, so any range can be
+    generated on its own); threads > 1 (or 0 = all cores) splits the range, same values."""
     out = np.empty(n, np.float32)
-    lib().or_cfg_fill(_p(out), first, n, seed, stream, dist, p0, p1)
+    if threads == 1:
+        lib().or_cfg_fill(_p(out), first, n, seed, stream, dist, p0, p1)
+    else:
+        lib().or_cfg_fill_mt(_p(out), first, n, seed, stream, dist, p0, p1, threads)
     return out
 
 

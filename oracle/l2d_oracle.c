@@ -160,6 +160,43 @@ void or_cfg_fill(float *out, uint64_t first, uint64_t n, uint64_t seed, uint64_t
     for (uint64_t j = 0; j < n; ++j) out[j] = or_cfg_value(seed, stream, first + j, dist, p0, p1);
 }
 
+typedef struct {
+    float *out;
+    uint64_t first, n, seed, stream;
+    int dist;
+    float p0, p1;
+} or_fill_job;
+
+static void *or_fill_worker(void *arg) {
+    or_fill_job *j = (or_fill_job *)arg;
+    or_cfg_fill(j->out, j->first, j->n, j->seed, j->stream, j->dist, j->p0, j->p1);
+    return NULL;
+}
+
+/* or_cfg_fill with the index range split over `threads` POSIX threads (0 = all online cores);
+ * every value depends on its index only, so the output equals the single-threaded fill. */
+void or_cfg_fill_mt(float *out, uint64_t first, uint64_t n, uint64_t seed, uint64_t stream, int dist, float p0, float p1,
+                    int threads) {
+    int nt = threads > 0 ? threads : (int)sysconf(_SC_NPROCESSORS_ONLN);
+    if (nt < 1) nt = 1;
+    if (nt > 256) nt = 256;
+    if ((uint64_t)nt > n / 65536 + 1) nt = (int)(n / 65536 + 1);
+    or_fill_job jobs[256];
+    pthread_t tids[256];
+    int started[256];
+    for (int t = 0; t < nt; ++t) {
+        const uint64_t lo = n * (uint64_t)t / (uint64_t)nt, hi = n * (uint64_t)(t + 1) / (uint64_t)nt;
+        or_fill_job j = {out + lo, first + lo, hi - lo, seed, stream, dist, p0, p1};
+        jobs[t] = j;
+        started[t] = t > 0 && pthread_create(&tids[t], NULL, or_fill_worker, &jobs[t]) == 0;
+    }
+    or_fill_worker(&jobs[0]);
+    for (int t = 1; t < nt; ++t) {
+        if (started[t]) pthread_join(tids[t], NULL);
+        else or_fill_worker(&jobs[t]);
+    }
+}
+
 /* ------------------------------------------------------------------------------------------ */
 /* Storage formats.                                                                            */
 /* ------------------------------------------------------------------------------------------ */

@@ -38,6 +38,9 @@ double or_cos_2pi(double u);     /* cos(2*pi*u) for u in [0, 1), Taylor series a
 /* dist UNIFORM: p0 + (p1 - p0) * u;  dist NORMAL: p1 * N(0,1) + p0 (p0 = mean, p1 = sigma). */
 float or_cfg_value(uint64_t seed, uint64_t stream, uint64_t index, int dist, float p0, float p1);
 void or_cfg_fill(float *out, uint64_t first, uint64_t n, uint64_t seed, uint64_t stream, int dist, float p0, float p1);
+/* The same values, computed by `threads` threads (0 = all online cores). */
+void or_cfg_fill_mt(float *out, uint64_t first, uint64_t n, uint64_t seed, uint64_t stream, int dist, float p0, float p1,
+                    int threads);
 
 /* ---- storage formats (IEEE round-to-nearest-even, integer code) ---- */
 uint16_t or_f32_to_f16(float f);

@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate tests/golden/reference_pins.json from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference, override with
-L2D_REFERENCE_ROOT):
+Run where the reference tree is present (L2D_REFERENCE_ROOT, else a `reference` directory beside
+this repository):
 
     make -C oracle ref            # compiles the reference's GEMV source in place -> oracle/_ref/
     python tests/golden/make_golden.py
@@ -35,7 +35,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("L2D_REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("L2D_REFERENCE_ROOT") or os.path.join(os.path.dirname(REPO), "reference")
 PIN = os.path.join(REPO, "oracle", "_ref", "libref_pin.so")
 OUT = os.path.join(HERE, "reference_pins.json")
 

@@ -109,3 +109,11 @@ def test_reference_rules_on_h100_fixtures():
     # latopt.cuh:528 on a near-only and a mixed trace.
     assert O.ref_smid_side([280] * 16) == 0
     assert O.ref_smid_side([280] * 8 + [460] * 8) == 1
+
+
+def test_threaded_fill_equals_sequential_fill():
+    """The threaded generator (used by the full-size GPU parity tests) gives the same values."""
+    for dist, p0, p1 in ((O.UNIFORM, -1.0, 1.0), (O.NORMAL, 0.0, 0.02)):
+        a = O.cfg_fill(300_001, 0, 0, dist, p0, p1, first=12_345)
+        b = O.cfg_fill(300_001, 0, 0, dist, p0, p1, first=12_345, threads=7)
+        assert np.array_equal(a, b)

@@ -138,6 +138,82 @@ def _two_gpu_worker(rank, world, port, M, N, q):
         dist.destroy_process_group()
 
 
+def _cfg5_worker(rank, world, port, M, N, rows_sample, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from l2domain_b200.shard import PeerGemvStep, exchange_bytes
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        shard = RowShard(M, world, rank)
+        keep, A = aligned(shard.rows * N * 2, dev)
+        L.fill_cfg(A, L.F16, shard.rows * N, 0, 0, 1, 0.0, 0.02, first=shard.row0 * N)
+        plan = L.GemvPlan(A, shard.rows, N, L.F16, L.F16, device=rank)
+        step = PeerGemvStep(shard, plan, N, L.F16, L.F16, rank, lambda b: exchange_bytes(b, device=dev))
+        out = {}
+        for mode in (L.MODE_AWARE, L.MODE_STREAM):
+            for k in range(2):
+                par = step.next_parity()
+                if rank == 0:
+                    L.fill_cfg(step.x(par), L.F16, N, 0, 1, 1, 0.0, 1.0)
+                step(mode)
+                torch.cuda.synchronize()
+            out[mode] = step.y(par).view(torch.int16)[torch.as_tensor(rows_sample, device=dev)].cpu().numpy()
+        st = step.status()
+        dist.barrier(device_ids=[rank])
+        step.close()
+        plan.close()
+        q.put((rank, out, st))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_all_gpus_cfg5_gathered_y_matches_oracle():
+    """Config 5 at full size (fp16 A 131072 x 16384, 4 GiB) row-sharded over every visible GPU,
+    two steps per mode with x from rank 0: on every rank, the gathered y of sampled rows of every
+    rank's shard (its first, middle and last 64 rows) is checked against the CPU oracle (relative
+    L2 <= 2e-3 of the fp64 result of the same rounded inputs), and all ranks hold the same bits."""
+    need_gpu(2)
+    import numpy as np
+    import torch.multiprocessing as mp
+
+    import oracle as O
+
+    M, N, world = 131072, 16384, torch.cuda.device_count()
+    shards = [RowShard(M, world, r) for r in range(world)]
+    rows = np.unique(np.concatenate([np.r_[s.row0: s.row0 + 64, s.row0 + s.rows // 2 - 32: s.row0 + s.rows // 2 + 32,
+                                           s.row0 + s.rows - 64: s.row0 + s.rows] for s in shards]))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cfg5_worker, args=(r, world, port, M, N, rows, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    x_h = O.round_to(O.cfg_fill(N, 0, 1, O.NORMAL, 0.0, 1.0), O.F16)
+    runs = np.split(rows, np.where(np.diff(rows) != 1)[0] + 1)
+    y64 = np.concatenate([O.gemv_f64(O.round_to(O.cfg_fill(len(r) * N, 0, 0, O.NORMAL, 0.0, 0.02,
+                                                           first=int(r[0]) * N, threads=0), O.F16),
+                                     x_h, O.F16, len(r), N) for r in runs])
+    ref = O.round_out(y64, O.F16).astype(np.float64)
+    results = dict((r, (o, s)) for r, o, s in (q.get(timeout=600) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        outs, st = results[r]
+        assert st == 0, f"rank {r} timeout bits {st}"
+        for mode, y in outs.items():
+            got = O.widen(y.view(np.uint16), O.F16)
+            err = O.rel_l2(ref, got)
+            assert err <= 2e-3, f"rank {r} mode {mode}: rel L2 {err:.3g}"
+            assert np.array_equal(y, results[0][0][mode]), f"rank {r} mode {mode}: differs from rank 0"
+
+
 @pytest.mark.parametrize("M", [5003, 1])
 def test_two_gpus_gather_equals_nccl_allgather(M):
     """M = 1 leaves rank 1 without rows: it still takes part in every step."""
