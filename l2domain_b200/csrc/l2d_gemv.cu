@@ -74,6 +74,7 @@ struct GemvArgs {
     int x_smem;                   // 1 = stage the slot's x vectors in shared memory
     int ring_off;                 // TMA kernels: byte offset of the granule rings in dynamic shared memory
     int use_tma;                  // 1 = this call runs the granule-ring kernel
+    int x_glob;                   // ring kernels, batched calls: x read from global memory (through L1) per problem
     const int32_t *sm_slot;       // [kMaxSmid] slot of each SM, -1 = none
     int n_slots;
     int n_dom0;
@@ -705,6 +706,7 @@ template <bool SPLIT> struct PoolWalker {
     uint32_t mask;          // granules of the current row still to fetch
     bool whole;
     const uint8_t *rowp;
+    int xbase;              // byte offset of the current row's x from a.x (batched calls; 0 otherwise)
 
     __device__ __forceinline__ void start(const GemvArgs &a, int grp_, long long k_first, long long k_second) {
         grp = grp_;
@@ -717,6 +719,7 @@ template <bool SPLIT> struct PoolWalker {
         mask = 0u;
         whole = false;
         rowp = nullptr;
+        xbase = 0;
     }
 
     // The next chunk: a chunk of the first claim, the claim in flight, or a new one; when a pool
@@ -757,7 +760,14 @@ template <bool SPLIT> struct PoolWalker {
     __device__ __forceinline__ bool next(const GemvArgs &a, int lane, uint8_t *stage, uint64_t *bar, TmaMeta *meta) {
         while (mask == 0u) {
             if (row >= end && !take_chunk(a, lane)) return false;
-            rowp = a.A + row * a.lda_bytes;
+            if (a.x_glob) {  // batched: problem b = row / M (rows_total < 2^31)
+                const int32_t M = static_cast<int32_t>(a.M), r = static_cast<int32_t>(row);
+                const int32_t b = r / M;
+                rowp = a.A + b * a.stride_a_bytes + static_cast<int64_t>(r - b * M) * a.lda_bytes;
+                xbase = static_cast<int>(b * a.stride_x_bytes);
+            } else {
+                rowp = a.A + row * a.lda_bytes;
+            }
             bool own = lane < G;
             if (SPLIT && pool == 0 && own) {
                 const uint64_t u = (static_cast<uint64_t>(rowp - a.region_base) >> kUnitShift) +
@@ -772,7 +782,7 @@ template <bool SPLIT> struct PoolWalker {
         mask &= mask - 1u;
         if (lane == 0) {
             meta->row = static_cast<int>(row);
-            meta->xoff = g * kGranBytes;
+            meta->xoff = xbase + g * kGranBytes;
             meta->last = (mask == 0u ? 1 : 0) | (whole ? 2 : 0);
             mbar_expect_tx(bar, kGranBytes);
             bulk_to_smem(stage, rowp + static_cast<int64_t>(g) * kGranBytes, kGranBytes, bar);
@@ -799,12 +809,21 @@ struct Pending {
     unsigned long long old = 0ull;
 };
 
+// Element offset of ring-call row r in y: r for one problem, problem r / M at stride_y otherwise
+// (rows_total < 2^31, so 32-bit division).
+__device__ __forceinline__ int64_t ring_y_index(const GemvArgs &a, int64_t r) {
+    if (!a.x_glob) return r;
+    const int32_t M = static_cast<int32_t>(a.M), r32 = static_cast<int32_t>(r);
+    const int32_t b = r32 / M;
+    return b * a.stride_y_elems + (r32 - b * M);
+}
+
 template <int DT_OUT, bool SH> __device__ __forceinline__ void resolve(const GemvArgs &a, Pending &p, uint32_t tag) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
     if (p.row < 0) return;
     if (static_cast<uint32_t>(p.old >> 32) == tag) {
         const float v = p.sum + __uint_as_float(static_cast<uint32_t>(p.old));
-        store_out<DT_OUT>(a.y + p.row * eo, v);
+        store_out<DT_OUT>(a.y + ring_y_index(a, p.row) * eo, v);
         final_to_peers<DT_OUT, SH>(a, p.row, v);
         a.xch[p.row] = 0ull;
     }
@@ -854,18 +873,33 @@ __device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long
             break;
         }
         const uint8_t *st = stages + s * kGranBytes;
-        const uint8_t *xg = xs + m.xoff;
+        if (a.x_glob) {  // batched: this problem's x through L1 (the warps of an SM share one or two problems)
+            const uint8_t *xg = a.x + m.xoff;
 #pragma unroll
-        for (int u = 0; u < kGranBytes >> kUnitShift; ++u) {
-            const int o = (u << kUnitShift) + lane * 16;
-            const uint4 a0 = *reinterpret_cast<const uint4 *>(st + o);
-            const uint4 a1 = *reinterpret_cast<const uint4 *>(st + o + 512);
-            const uint4 x0 = *reinterpret_cast<const uint4 *>(xg + o);
-            const uint4 x1 = *reinterpret_cast<const uint4 *>(xg + o + 512);
-            Vec32 av;
-            av.v[0] = a0.x, av.v[1] = a0.y, av.v[2] = a0.z, av.v[3] = a0.w;
-            av.v[4] = a1.x, av.v[5] = a1.y, av.v[6] = a1.z, av.v[7] = a1.w;
-            acc.unit(av, x0, x1);
+            for (int u = 0; u < kGranBytes >> kUnitShift; ++u) {
+                const int o = (u << kUnitShift) + lane * 16;
+                const uint4 x0 = ld_x16(xg + o, false), x1 = ld_x16(xg + o + 512, false);
+                const uint4 a0 = *reinterpret_cast<const uint4 *>(st + o);
+                const uint4 a1 = *reinterpret_cast<const uint4 *>(st + o + 512);
+                Vec32 av;
+                av.v[0] = a0.x, av.v[1] = a0.y, av.v[2] = a0.z, av.v[3] = a0.w;
+                av.v[4] = a1.x, av.v[5] = a1.y, av.v[6] = a1.z, av.v[7] = a1.w;
+                acc.unit(av, x0, x1);
+            }
+        } else {
+            const uint8_t *xg = xs + m.xoff;
+#pragma unroll
+            for (int u = 0; u < kGranBytes >> kUnitShift; ++u) {
+                const int o = (u << kUnitShift) + lane * 16;
+                const uint4 a0 = *reinterpret_cast<const uint4 *>(st + o);
+                const uint4 a1 = *reinterpret_cast<const uint4 *>(st + o + 512);
+                const uint4 x0 = *reinterpret_cast<const uint4 *>(xg + o);
+                const uint4 x1 = *reinterpret_cast<const uint4 *>(xg + o + 512);
+                Vec32 av;
+                av.v[0] = a0.x, av.v[1] = a0.y, av.v[2] = a0.z, av.v[3] = a0.w;
+                av.v[4] = a1.x, av.v[5] = a1.y, av.v[6] = a1.z, av.v[7] = a1.w;
+                acc.unit(av, x0, x1);
+            }
         }
         if (m.last & 1) {
             float sum = acc.total();
@@ -874,7 +908,7 @@ __device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long
             if (lane == 0) {
                 const int64_t row = m.row;
                 if (!SPLIT || (m.last & 2)) {
-                    store_out<DT_OUT>(a.y + row * eo, sum);
+                    store_out<DT_OUT>(a.y + ring_y_index(a, row) * eo, sum);
                     final_to_peers<DT_OUT, SH>(a, row, sum);
                 } else {
                     resolve<DT_OUT, SH>(a, pend, tag);
@@ -955,7 +989,7 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
     const int first = a.first_chunks[grp];
     if (tid == 0 && first > 0)
         s_k0 = static_cast<long long>(atomicAdd(pool_counter(a, SPLIT ? 0 : 1, grp), static_cast<unsigned long long>(first)));
-    if (!SH) stage_x_issue(a, smem);
+    if (!SH && !a.x_glob) stage_x_issue(a, smem);
     // The attr words reach L1 while the first claim is in flight: the first ballot of every warp
     // reads them before its first copy can start.
     if (SPLIT && a.dom_kind == 0 && tid < (a.attr_words + 31) / 32)
@@ -1212,6 +1246,7 @@ struct l2d_plan {
     bool tma = false;         // granule-ring kernels are available (TMA bulk copies of A)
     bool tma_force = false;   // L2D_PLAN_TMA: use them for every mode
     size_t ring_off = 0;      // their ring block's offset in dynamic shared memory
+    bool ring_xglob = false;  // batched ring calls: x read from global memory per problem
     unsigned long long *d_claim = nullptr;
     unsigned long long *d_ctl = nullptr;
 };
@@ -1441,6 +1476,21 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
             p->ring_off = ring_off;
         }
     }
+    // Batched problems on the granule-ring kernels: every problem's rows on 4 KiB granules, at most
+    // 32 granules per row, x read per problem through L1 (byte offsets of x below 2^31).
+    if (!(d.flags & L2D_PLAN_NO_TMA) && d.batch > 1 && d.M > 0 && d.N > 0 &&
+        !(reinterpret_cast<uintptr_t>(d.A) & (kGranBytes - 1)) && (d.N * eb) % kGranBytes == 0 &&
+        d.N * eb <= 32 * kGranBytes && (d.lda * eb) % kGranBytes == 0 && (d.stride_a * eb) % kGranBytes == 0 &&
+        d.batch * d.stride_x * eb < (int64_t(1) << 31) && (!p->has_domains || p->gran_shift >= kGranShift)) {
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, d.device);
+        if (kTmaBlockBytes + 1024 <= static_cast<size_t>(optin)) {
+            p->tma = true;
+            p->tma_force = (d.flags & L2D_PLAN_TMA) != 0;
+            p->ring_off = 0;
+            p->ring_xglob = true;
+        }
+    }
     for (int v = 0; v < 8; ++v) {
         const int fe = allow_max_smem(pick_kernel(d.dtype_in, d.dtype_out, v & 1, (v >> 1) & 1, v >> 2), d.device);
         if (fe != L2D_OK) {
@@ -1574,6 +1624,7 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.x_smem = p->x_smem_bytes > 0;
     a.ring_off = static_cast<int>(p->ring_off);
     a.use_tma = use_ring(p, split) ? 1 : 0;
+    a.x_glob = a.use_tma && p->ring_xglob ? 1 : 0;
     a.xch = p->d_xch;
     const RingPools rp = ring_pools(p, split, mode);
     a.whole_lo = rp.whole_lo;
@@ -1602,7 +1653,8 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
 // (a call that reaches the kernel with a missing scratch pointer is refused, never launched).
 int check_args(const GemvArgs &a) {
     if (!a.x || !a.y || !a.sm_slot || !a.part || !a.meet || !a.claim || !a.ctl || a.n_slots <= 0 ||
-        (a.use_tma && (!a.xch || a.pool_chunk <= 0 || a.whole_lo < 0 || a.whole_lo > a.rows_total || !a.x_smem)) ||
+        (a.use_tma && (!a.xch || a.pool_chunk <= 0 || a.whole_lo < 0 || a.whole_lo > a.rows_total ||
+                       (!a.x_smem && !a.x_glob) || (a.x_glob && a.row_bytes <= 0))) ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");
     if (a.shard_world > 1 && (!a.peer_xw || !a.peer_yw || !a.shard_status || !a.x_smem || a.rows_total != a.M ||

@@ -168,6 +168,46 @@ int fill_grid(uint64_t n) {
 std::mutex g_flush_mu;
 std::map<int, std::pair<void *, size_t>> g_flush;  // device -> flush buffer (kept until exit)
 
+// Read-only stream: every 32-byte chunk of [p, p + n32 * 32) is loaded once (256-bit non-coherent
+// loads that do not allocate in L1, 4 in flight per thread, 128 KiB per SM) and folded into one
+// XOR word per CTA, so the loads cannot be elided.  The roofline denominators for a read-dominated
+// kernel: over a buffer larger than L2 it gives the HBM read bandwidth, over an L2-resident buffer
+// read back to back the L2 read bandwidth.
+__global__ void __launch_bounds__(1024) k_read_stream(const uint8_t *p, uint64_t n32, uint32_t *sink) {
+    constexpr int kU = 4;
+    uint32_t acc = 0;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + (kU - 1) * stride < n32; i += kU * stride) {
+        uint32_t v[kU][8];
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                         : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3]), "=r"(v[u][4]), "=r"(v[u][5]),
+                           "=r"(v[u][6]), "=r"(v[u][7])
+                         : "l"(p + (i + u * stride) * 32));
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc ^= v[u][k];
+    }
+    for (; i < n32; i += stride) {
+        const uint4 *q = reinterpret_cast<const uint4 *>(p + i * 32);
+        const uint4 a = __ldg(q), b = __ldg(q + 1);
+        acc ^= a.x ^ a.y ^ a.z ^ a.w ^ b.x ^ b.y ^ b.z ^ b.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc ^= __shfl_xor_sync(0xffffffffu, acc, o);
+    __shared__ uint32_t s[32];
+    if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t t = 0;
+        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t ^= s[w];
+        sink[blockIdx.x] = t;
+    }
+}
+
 }  // namespace gen
 }  // namespace l2d
 
@@ -221,6 +261,26 @@ int l2d_l2_flush(int device, void *stream_handle) {
     cudaError_t e = cudaMemsetAsync(buf.first, 0, buf.second, static_cast<cudaStream_t>(stream_handle));
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "l2_flush: %s", cudaGetErrorString(e));
+    return L2D_OK;
+}
+
+int l2d_read_stream(int device, const void *p, size_t bytes, uint32_t *sink, size_t sink_words, void *stream_handle) {
+    clear_error();
+    if (!p || !sink || (reinterpret_cast<uintptr_t>(p) & 31) || (bytes & 31))
+        return set_error(L2D_ERR_INVALID, "read_stream: p must be 32-byte aligned and bytes a multiple of 32");
+    int num_sm = 0;
+    L2D_CUDA_TRY(cudaDeviceGetAttribute(&num_sm, cudaDevAttrMultiProcessorCount, device));
+    if (sink_words < static_cast<size_t>(num_sm))
+        return set_error(L2D_ERR_INVALID, "read_stream: sink holds %zu words, needs %d", sink_words, num_sm);
+    if (bytes == 0) return L2D_OK;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != device) L2D_CUDA_TRY(cudaSetDevice(device));
+    gen::k_read_stream<<<num_sm, 1024, 0, static_cast<cudaStream_t>(stream_handle)>>>(
+        static_cast<const uint8_t *>(p), bytes / 32, sink);
+    cudaError_t e = cudaGetLastError();
+    if (prev >= 0 && prev != device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "read_stream: %s", cudaGetErrorString(e));
     return L2D_OK;
 }
 

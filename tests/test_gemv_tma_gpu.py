@@ -6,8 +6,9 @@ bit-exact.  The ring kernels claim rows from pools, so the tests also pin what m
 who claimed what: AWARE and SWAPPED bit-identical on every split-pool row (the same two partials,
 added commutatively), rows taken whole bit-identical with STREAM (one warp, granules in order),
 repeated calls bit-identical whatever ran in between (the exchange words empty themselves, the pool
-counters reset).  Shapes the ring kernels cannot take (rows off the 4 KiB granules, batched
-problems) run the register kernels.
+counters reset).  Batched calls run the ring kernels too when every problem's rows sit on 4 KiB
+granules (x then comes through L1 per problem); shapes the ring kernels cannot take (rows or
+problem strides off the 4 KiB granules) run the register kernels.
 """
 import json
 import os
@@ -162,14 +163,75 @@ def test_ring_kernels_agree_with_register_kernels(dev):
     assert np.linalg.norm(a - b) / np.linalg.norm(b) <= 1e-5
 
 
-def test_batched_problems_run_register_kernels(dev):
-    M, N, batch = 300, 4096, 3  # granule-aligned rows and problem stride, but three problems
-    A, x = inputs(M, N, L.F16, batch)
-    outs, stats = run(A, x, M, N, L.F16, L.F16, ALL_MODES, batch)
-    assert stats["tma"] == 0
-    ref = oracle(A, x, L.F16, M, N, batch, L.F16)
+@pytest.mark.parametrize("M,N,dtype,dtype_out,batch,pad_a,pad_x,pad_y", [
+    (300, 4096, L.F16, L.F16, 3, 0, 0, 0),          # contiguous batch, 8 KiB rows
+    (1000, 8192, L.BF16, L.BF16, 5, 4096, 24, 7),   # problem stride padded by one granule, x and y padded
+    (64, 2048, L.F32, L.F32, 9, 8192, 4, 1),        # few rows per problem: chunks straddle problems
+    (5, 16384, L.F16, L.F32, 40, 0, 8, 3),          # 32 KiB rows, more problems than rows per problem
+])
+def test_batched_ring_kernels_match_oracle(dev, M, N, dtype, dtype_out, batch, pad_a, pad_x, pad_y):
+    """Batched calls on the granule-ring kernels (every problem's rows on 4 KiB granules): x of each
+    problem is read through L1, y of problem b lands at b * stride_y."""
+    eb = L.ELEM_BYTES[dtype]
+    sa, sx, sy = M * N + pad_a // eb, N + pad_x, M + pad_y
+    n_a, n_x = (batch - 1) * sa + M * N, (batch - 1) * sx + N
+    A_h = O.round_to(O.cfg_fill(n_a, 1, 0, O.NORMAL, 0.0, 0.02), dtype)
+    x_h = O.round_to(O.cfg_fill(n_x, 1, 1, O.NORMAL, 0.0, 1.0), dtype)
+    raw = torch.empty(A_h.nbytes + PAGE, dtype=torch.uint8, device="cuda")
+    off = (-raw.data_ptr()) % PAGE
+    A = raw[off: off + A_h.nbytes]
+    A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
+    x = to_dev(x_h)
+    plan = L.GemvPlan(A, M, N, dtype, dtype_out, batch=batch, stride_a=sa, stride_x=sx, stride_y=sy, tma=True)
+    st = plan.stats()
+    assert st["tma"] == 2 and st["ring_modes"] == 0b1111
+    y64 = np.concatenate([O.gemv_f64(A_h[b * sa: b * sa + M * N], x_h[b * sx: b * sx + N], dtype, M, N)
+                          for b in range(batch)])
+    ref = (O.round_out(y64, dtype_out) if dtype_out != L.F32 else y64).astype(np.float64)
+    rows = np.concatenate([np.arange(b * sy, b * sy + M) for b in range(batch)])
+    n_y = (batch - 1) * sy + M
     for m in ALL_MODES:
-        assert O.rel_l2(ref.astype(np.float64), outs[m]) <= TOL[L.F16]
+        if dtype_out == L.F32:
+            y = torch.full((n_y,), float("nan"), dtype=torch.float32, device="cuda")
+        else:
+            y = torch.full((n_y,), -1, dtype=torch.int16, device="cuda")
+        plan.gemv(A, x, y, m)
+        torch.cuda.synchronize()
+        yh = y.cpu().numpy()
+        got = yh if dtype_out == L.F32 else O.widen(yh.view(np.uint16), dtype_out)
+        err = O.rel_l2(ref, got[rows])
+        assert err <= TOL[dtype], f"mode {m}: rel L2 {err:.3g}"
+        pad = np.setdiff1d(np.arange(n_y), rows)  # rows between problems are never written
+        if dtype_out == L.F32:
+            assert np.all(np.isnan(yh[pad]))
+        else:
+            assert np.all(yh[pad] == -1)
+    st = plan.stats()
+    assert st["device_errors"] == 0
+    plan.close()
+
+
+def test_batched_off_granule_stride_runs_register_kernels(dev):
+    M, N, batch = 300, 4096, 3  # problem stride not a multiple of 4 KiB
+    sa = M * N + 8
+    A_h = O.round_to(O.cfg_fill((batch - 1) * sa + M * N, 2, 0, O.NORMAL, 0.0, 0.02), L.F16)
+    x_h = O.round_to(O.cfg_fill(batch * N, 2, 1, O.NORMAL, 0.0, 1.0), L.F16)
+    raw = torch.empty(A_h.nbytes + PAGE, dtype=torch.uint8, device="cuda")
+    off = (-raw.data_ptr()) % PAGE
+    A = raw[off: off + A_h.nbytes]
+    A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
+    x = to_dev(x_h)
+    plan = L.GemvPlan(A, M, N, L.F16, L.F16, batch=batch, stride_a=sa)
+    assert plan.stats()["tma"] == 0
+    y64 = np.concatenate([O.gemv_f64(A_h[b * sa: b * sa + M * N], x_h[b * N:(b + 1) * N], L.F16, M, N)
+                          for b in range(batch)])
+    for m in ALL_MODES:
+        y = torch.full((batch * M,), -1, dtype=torch.int16, device="cuda")
+        plan.gemv(A, x, y, m)
+        torch.cuda.synchronize()
+        got = O.widen(y.cpu().numpy().view(np.uint16), L.F16)
+        assert O.rel_l2(O.round_out(y64, L.F16).astype(np.float64), got) <= TOL[L.F16]
+    plan.close()
 
 
 def test_unaligned_rows_fall_back_to_register_kernels(dev):
