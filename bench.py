@@ -221,6 +221,193 @@ def run_reference(args, rank, world):
 
 
 # ------------------------------------------------------------------------------------------------
+# Timing helpers and the side measurements of the other configs
+# ------------------------------------------------------------------------------------------------
+
+MODE_NAMES = (("aware", 1), ("oblivious", 0), ("swapped", 2), ("stream", 3))
+
+
+def kernel_time_us(fn, steps, stream, barrier=None, reduce=None, warm=3):
+    """Mean µs per call of `steps` back-to-back calls between one event pair on `stream`."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    (barrier or torch.cuda.synchronize)()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    b.synchronize()
+    us = a.elapsed_time(b) / steps * 1e3
+    return reduce(us) if reduce else us
+
+
+def flushed_call_us(fn, y, L, device, stream, runs=20, warm=5):
+    """The reference's timing protocol (applications/gemv/src/gemv_k1024_persistent_subwarp.cu:279-355):
+    `warm` warm-up calls, then per call: y cleared, L2 flushed, a device sync, one event pair around
+    the single launch; the mean over `runs`."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    for _ in range(runs):
+        y.zero_()
+        L.l2_flush(device, stream)
+        torch.cuda.synchronize()
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total / runs * 1e3
+
+
+def cublas_cli_us(M, N, dt, runs, warm, flush):
+    """µs per call of the cuBLAS comparator binary (gemv_cublas_benchmark, the reference's cuBLAS
+    column: one event pair per call, L2 flushed before each when flush=1)."""
+    import subprocess
+
+    exe = os.path.join(REPO, "l2domain_b200", "bin", "gemv_cublas_benchmark")
+    try:
+        r = subprocess.run([exe, str(M), str(N), str(runs), str(warm), str(flush), DT_NAME[dt]], capture_output=True,
+                           text=True, timeout=300)
+    except (OSError, subprocess.TimeoutExpired):
+        return None
+    for line in r.stdout.splitlines():
+        t = line.split()
+        if t and t[0] == "cublas_ms":
+            return round(float(t[1]) * 1e3, 3)
+    return None
+
+
+def aligned_buffer(torch, dev, nbytes):
+    raw = torch.empty(nbytes + (2 << 20), dtype=torch.uint8, device=dev)
+    off = (-raw.data_ptr()) % (2 << 20)
+    return raw, raw[off: off + nbytes]
+
+
+def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
+    """µs and GB/s per mode for configs 1-4 and the L2-window shape on this GPU, next to cuBLAS."""
+    tdt = {F32: torch.float32, F16: torch.float16, BF16: torch.bfloat16}
+    sink = torch.empty(4096, dtype=torch.int32, device=dev)
+    out = {}
+
+    def setup(M, N, dt, adist, xdist, batch=1):
+        raw, A = aligned_buffer(torch, dev, batch * M * N * EB[dt])
+        L.fill_cfg(A, dt, batch * M * N, 0, 0, *adist)
+        x = torch.empty(batch * N * EB[dt], dtype=torch.uint8, device=dev)
+        L.fill_cfg(x, dt, batch * N, 0, 1, *xdist)
+        y = torch.empty(batch * M * EB[dt], dtype=torch.uint8, device=dev)
+        plan = L.GemvPlan(A, M, N, dt, dt, batch=batch, device=local)
+        return raw, A, x, y, plan
+
+    def per_mode(plan, A, x, y, calls):
+        return {name: round(kernel_time_us(lambda m=mode: plan.gemv(A, x, y, m, stream), calls, stream), 3)
+                for name, mode in MODE_NAMES}
+
+    def gbs(nbytes, us):
+        return {k: round(nbytes / (v * 1e-6) / 1e9, 1) for k, v in us.items() if v}
+
+    def read_gbs(buf, nbytes, calls):
+        nb = nbytes // 32 * 32
+        return round(nb / (kernel_time_us(lambda: L.read_stream(buf, nb, sink, 4096, local, stream), calls, stream)
+                           * 1e-6) / 1e9, 1)
+
+    # Config 2: L2-resident fp16 4096x4096, 1000 back-to-back calls, against the L2 read peak.
+    M, N, dt = 4096, 4096, F16
+    raw, A, x, y, plan = setup(M, N, dt, (NORMAL, 0.0, 0.02), (NORMAL, 0.0, 1.0))
+    nbytes = M * N * 2 + N * 2 + M * 2
+    l2_peak = read_gbs(A, M * N * 2, 1000)
+    us = per_mode(plan, A, x, y, 1000)
+    A2, xv, yv = A.view(tdt[dt]).view(M, N), x.view(tdt[dt]), y.view(tdt[dt])
+    us["cublas_torch_mv"] = round(kernel_time_us(lambda: torch.mv(A2, xv, out=yv), 1000, stream), 3)
+    g = gbs(nbytes, us)
+    out["cfg2"] = {"workload": "fp16 4096x4096 (32 MiB), 1000 back-to-back calls, no flush (L2-resident)",
+                   "bound": "l2", "us": us, "gbs": g, "l2_read_peak_gbs": l2_peak,
+                   "frac_of_l2_read_peak": {k: round(v / l2_peak, 4) for k, v in g.items()},
+                   "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 200, 20, 0)}
+    plan.close()
+    del raw, A
+
+    # The L2 window: fp16 3584x16384 (112 MiB) fits in the two L2 halves only when each half keeps
+    # its own domain's lines, so the near-domain split shows here.
+    M, N, dt = 3584, 16384, F16
+    raw, A, x, y, plan = setup(M, N, dt, (NORMAL, 0.0, 0.02), (NORMAL, 0.0, 1.0))
+    us = per_mode(plan, A, x, y, 500)
+    g = gbs(M * N * 2 + N * 2 + M * 2, us)
+    out["l2_window"] = {"workload": "fp16 3584x16384 (112 MiB), 500 back-to-back calls, no flush", "bound": "l2",
+                        "us": us, "gbs": g, "read_stream_gbs": read_gbs(A, M * N * 2, 500),
+                        "aware_speedup_vs_stream": round(us["stream"] / us["aware"], 4),
+                        "aware_speedup_vs_oblivious": round(us["oblivious"] / us["aware"], 4),
+                        "swapped_slowdown_vs_aware": round(us["swapped"] / us["aware"], 4)}
+    plan.close()
+    del raw, A
+
+    # Config 1: fp32 4096x4096 U[-1,1], the reference protocol (L2 flushed, one event pair per call)
+    # and back to back (64 MiB stays in L2).
+    M, N, dt = 4096, 4096, F32
+    raw, A, x, y, plan = setup(M, N, dt, (UNIFORM, -1.0, 1.0), (UNIFORM, -1.0, 1.0))
+    nbytes = M * N * 4 + N * 4 + M * 4
+    A2, xv, yv = A.view(torch.float32).view(M, N), x.view(torch.float32), y.view(torch.float32)
+    flushed = {name: round(flushed_call_us(lambda m=mode: plan.gemv(A, x, y, m, stream), y, L, local, stream), 3)
+               for name, mode in MODE_NAMES}
+    flushed["cublas_torch_mv"] = round(flushed_call_us(lambda: torch.mv(A2, xv, out=yv), y, L, local, stream), 3)
+    flushed["cublas_cli"] = cublas_cli_us(M, N, dt, 20, 5, 1)
+    steady = per_mode(plan, A, x, y, 200)
+    steady["cublas_torch_mv"] = round(kernel_time_us(lambda: torch.mv(A2, xv, out=yv), 200, stream), 3)
+    gf = gbs(nbytes, flushed)
+    out["cfg1"] = {"workload": "fp32 4096x4096 (64 MiB), U[-1,1] seed 0",
+                   "reference_protocol": {"protocol": "5 warm-ups, then per call: y cleared, L2 flushed, sync, one "
+                                                      "event pair around the launch; mean of 20", "bound": "hbm",
+                                          "us": flushed, "gbs": gf,
+                                          "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in gf.items()}
+                                          if read_peak else None},
+                   "back_to_back": {"protocol": "200 back-to-back calls, no flush (64 MiB stays in L2)", "bound": "l2",
+                                    "us": steady, "gbs": gbs(nbytes, steady)}}
+    plan.close()
+    del raw, A
+
+    # Config 3: bf16 28672x8192 (448 MiB, larger than L2), 50 back-to-back calls.
+    M, N, dt = 28672, 8192, BF16
+    raw, A, x, y, plan = setup(M, N, dt, (NORMAL, 0.0, 0.02), (NORMAL, 0.0, 1.0))
+    nbytes = M * N * 2 + N * 2 + M * 2
+    us = per_mode(plan, A, x, y, 50)
+    A2, xv, yv = A.view(torch.bfloat16).view(M, N), x.view(torch.bfloat16), y.view(torch.bfloat16)
+    us["cublas_torch_mv"] = round(kernel_time_us(lambda: torch.mv(A2, xv, out=yv), 50, stream), 3)
+    g = gbs(nbytes, us)
+    out["cfg3"] = {"workload": "bf16 28672x8192 (448 MiB), 50 back-to-back calls (inputs larger than L2)",
+                   "bound": "hbm", "us": us, "gbs": g,
+                   "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in g.items()} if read_peak else None,
+                   "frac_of_copy_peak": {k: round(v / copy_peak, 4) for k, v in g.items()},
+                   "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 20, 5, 0)}
+    plan.close()
+    del raw, A
+
+    # Config 4: batched fp16 32 x (8192x8192) (4 GiB), 10 back-to-back calls.
+    B, M, N, dt = 32, 8192, 8192, F16
+    raw, A, x, y, plan = setup(M, N, dt, (UNIFORM, -0.05, 0.05), (NORMAL, 0.0, 1.0), batch=B)
+    nbytes = B * (M * N * 2 + N * 2 + M * 2)
+    us = per_mode(plan, A, x, y, 10)
+    A3, x3, y3 = A.view(torch.float16).view(B, M, N), x.view(torch.float16).view(B, N, 1), \
+        y.view(torch.float16).view(B, M, 1)
+    us["cublas_torch_bmm"] = round(kernel_time_us(lambda: torch.bmm(A3, x3, out=y3), 10, stream), 3)
+    g = gbs(nbytes, us)
+    out["cfg4"] = {"workload": "fp16 32 x (8192x8192) contiguous batch (4 GiB), 10 back-to-back calls",
+                   "bound": "hbm", "us": us, "gbs": g,
+                   "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in g.items()} if read_peak else None,
+                   "kernel": "ring (TMA bulk copies)" if plan.stats()["ring_modes"] & 2 else "register"}
+    plan.close()
+    del raw, A
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
 # Our arm
 # ------------------------------------------------------------------------------------------------
 
@@ -355,9 +542,11 @@ def run_ours(args, rank, world, local):
     bidx = idx // m_loc
     ref = (Av[idx].double() * xv.view(batch, N)[bidx].double()).sum(1)
     got = y_loc.view(tdt)[idx].double()
-    rel = float(((got - ref).norm() / ref.norm()).item())
+    # Every rank checks 64 rows of its own shard; with the gathered y equal to the NCCL gather of the
+    # shards, that covers sampled rows of every rank's part of y.  The worst rank is reported.
+    rel = max_over_ranks(float(((got - ref).norm() / ref.norm()).item()))
     if not rel <= 2e-3:
-        raise SystemExit(f"rank {rank}: GEMV self-check failed, rel L2 {rel:.3g}")
+        raise SystemExit(f"rank {rank}: GEMV self-check failed, rel L2 {rel:.3g} (worst rank)")
 
     # Headline: K timed steps of the aware GEMV (plus the exchange at N > 1).  The clock sampler
     # starts before the warm-up so its thread and NVML are warm when the timed region begins.
@@ -396,19 +585,9 @@ def run_ours(args, rank, world, local):
     modes_us = {}
     if not args.no_aux:
         def kernel_time(fn, steps):
-            for _ in range(3):
-                fn()
-            barrier()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            for _ in range(steps):
-                fn()
-            b.record(stream)
-            b.synchronize()
-            return max_over_ranks(a.elapsed_time(b) / steps * 1e3)
+            return kernel_time_us(fn, steps, stream, barrier, max_over_ranks)
 
-        for name, mode in (("aware", L.MODE_AWARE), ("oblivious", L.MODE_OBLIVIOUS), ("swapped", L.MODE_SWAPPED),
-                           ("stream", L.MODE_STREAM)):
+        for name, mode in MODE_NAMES:
             modes_us[name] = round(kernel_time(lambda m=mode: plan.gemv(A, x, y_loc, m, stream), args.steps), 3)
         if batch == 1:
             out = torch.empty(m_loc, dtype=tdt, device=dev)
@@ -417,48 +596,20 @@ def run_ours(args, rank, world, local):
         Ai = A.view(torch.int64)
         modes_us["torch_sum_read"] = round(kernel_time(lambda: torch.sum(Ai), max(5, args.steps // 5)), 3)
 
-    # Side measurement, not the headline: config 2, the L2-resident fp16 4096x4096 GEMV (32 MiB),
-    # 1000 back-to-back calls per mode without a flush, where the near/far L2 latency shows.
-    l2res = None
+    # Read-only stream over this rank's A (larger than L2): the HBM read bandwidth of this box, the
+    # denominator beside the copy peak for a read-dominated kernel.
+    read_peak = None
+    if not args.no_aux:
+        sink = torch.empty(4096, dtype=torch.int32, device=dev)
+        rb = a_bytes // 32 * 32
+        read_us = kernel_time_us(lambda: L.read_stream(A, rb, sink, 4096, local, stream), max(5, args.steps // 5),
+                                 stream, barrier, max_over_ranks)
+        read_peak = round(rb / (read_us * 1e-6) / 1e9, 1)
+
+    # Side measurements of the other BASELINE configs (N=1 only): not the headline.
+    configs = None
     if not args.no_aux and world == 1:
-        m2, n2 = 4096, 4096
-        raw2 = torch.empty(m2 * n2 * 2 + (2 << 20), dtype=torch.uint8, device=dev)
-        o2 = (-raw2.data_ptr()) % (2 << 20)
-        A2b = raw2[o2: o2 + m2 * n2 * 2]
-        L.fill_cfg(A2b, F16, m2 * n2, 0, 0, NORMAL, 0.0, 0.02)
-        x2 = torch.empty(n2 * 2, dtype=torch.uint8, device=dev)
-        L.fill_cfg(x2, F16, n2, 0, 1, NORMAL, 0.0, 1.0)
-        y2 = torch.empty(m2 * 2, dtype=torch.uint8, device=dev)
-        plan2 = L.GemvPlan(A2b, m2, n2, F16, F16, device=local)
-        l2res = {"workload": "cfg2: fp16 4096x4096 (32 MiB, L2-resident), 1000 back-to-back calls, no flush"}
-        for name, mode in (("aware", L.MODE_AWARE), ("oblivious", L.MODE_OBLIVIOUS), ("swapped", L.MODE_SWAPPED),
-                           ("stream", L.MODE_STREAM)):
-            for _ in range(20):
-                plan2.gemv(A2b, x2, y2, mode, stream)
-            torch.cuda.synchronize()
-            a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a2.record(stream)
-            for _ in range(1000):
-                plan2.gemv(A2b, x2, y2, mode, stream)
-            b2.record(stream)
-            b2.synchronize()
-            l2res[f"{name}_us"] = round(a2.elapsed_time(b2), 3)  # ms for 1000 calls == us per call
-        A2m = A2b.view(torch.float16).view(m2, n2)
-        out2 = torch.empty(m2, dtype=torch.float16, device=dev)
-        xv2 = x2.view(torch.float16)
-        for _ in range(20):
-            torch.mv(A2m, xv2, out=out2)
-        torch.cuda.synchronize()
-        a2, b2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a2.record(stream)
-        for _ in range(1000):
-            torch.mv(A2m, xv2, out=out2)
-        b2.record(stream)
-        b2.synchronize()
-        l2res["cublas_torch_mv_us"] = round(a2.elapsed_time(b2), 3)
-        l2res["aware_gbs"] = round((m2 * n2 * 2 + n2 * 2 + m2 * 2) / (l2res["aware_us"] * 1e-6) / 1e9, 1)
-        plan2.close()
-        del raw2
+        configs = side_configs(L, torch, dev, local, stream, peak, read_peak)
 
     # End to end through the public API: pinned x in, y out, every step.
     x_host = torch.empty_like(x, device="cpu").pin_memory()
@@ -511,9 +662,12 @@ def run_ours(args, rank, world, local):
                        "dtype_in": DT_NAME[dt], "dtype_out": DT_NAME[dt], "rows_per_gpu": m_loc,
                        "parallelism": f"row-shard x{world}" + (exchange if world > 1 else ""),
                        "mode": "aware", "l2": f"inputs larger than L2 ({a_bytes / 2**20:.0f} MiB of A per GPU), no flush"},
-            "modes_us": modes_us, "aware_speedup_vs_oblivious": ratio, "l2_resident": l2res,
+            "modes_us": modes_us, "aware_speedup_vs_oblivious": ratio, "configs": configs,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src,
+                         "read_peak": read_peak,
+                         "read_peak_source": "measured in this run: l2d_read_stream over this rank's A, back to back",
+                         "frac_of_read_peak": round(achieved / read_peak, 4) if read_peak else None,
                          "frac_of_spec_8TBs": round(achieved / SPEC_HBM_GBS, 4), "kernel_us": round(kern_ms * 1e3, 3),
                          "bytes_per_launch": bytes_loc},
             "cpu_baseline": cpu,
@@ -527,7 +681,8 @@ def run_ours(args, rank, world, local):
                      "split_rows": pstats["split_rows"], "fallback_slots": fstats["fallback_slots"],
                      "calls": fstats["calls"],
                      "kernel": "ring (TMA bulk copies)" if fstats["ring_modes"] & (1 << L.MODE_AWARE) else "register"},
-            "check": {"rows": 64, "rel_l2_vs_f64": rel, "p2p_gather_equals_nccl": gather_exact},
+            "check": {"rows_per_rank": 64, "rel_l2_vs_torch_f64_worst_rank": rel,
+                      "p2p_gather_equals_nccl": gather_exact},
         }
         print(json.dumps(line), flush=True)
     if pstep is not None:

@@ -52,6 +52,9 @@ constexpr int kXSmemMax = 96 * 1024;
 #ifndef L2D_PDL
 #define L2D_PDL 1  // programmatic dependent launch of plan calls (0: plain stream order)
 #endif
+#ifndef L2D_CLAIM_EARLY
+#define L2D_CLAIM_EARLY 0  // 1: ring walks claim the next chunk with the first copy of a chunk's last row
+#endif
 
 struct GemvArgs {
     const uint8_t *A;
@@ -86,7 +89,8 @@ struct GemvArgs {
     unsigned int *meet;           // [n_slots] arrivals per interval of the two groups' slot partitions, zero between calls
     unsigned long long *xch;      // ring kernels: [rows_total] a split row's first partial and its call's tag (0 = empty)
     int64_t whole_lo;             // ring kernels: rows [whole_lo, rows_total) form the whole-row pool
-    int64_t pool_chunk;           // ring kernels: rows per pool claim
+    int64_t pool_chunk;           // ring kernels: rows per claim from the whole pool
+    int64_t pool_chunk_split;     // ring kernels: rows per claim from a group's split pool
     int first_chunks[2];          // ring kernels: chunks in the first claim of a group-g CTA (group 0: unsplit)
     uint32_t grp_bits[kMaxSmid / 32];  // ring kernels: bit s set = SM s belongs to domain group 1
     // Peer-memory row sharding (shard_world > 1; batch 1).  Every exchange is a flagged 8-byte
@@ -731,10 +735,11 @@ template <bool SPLIT> struct PoolWalker {
             const long long k = static_cast<long long>(__shfl_sync(0xffffffffu, v, 0));
             nxt_valid = false;
             const int64_t lo = pool ? a.whole_lo : 0, hi = pool ? a.rows_total : a.whole_lo;
-            const int64_t r = lo + k * a.pool_chunk;
+            const int64_t c = pool ? a.pool_chunk : a.pool_chunk_split;
+            const int64_t r = lo + k * c;
             if (r < hi) {
                 row = r;
-                end = min(r + a.pool_chunk, hi);
+                end = min(r + c, hi);
                 if (k2 >= 0) {
                     nxt = static_cast<unsigned long long>(k2);
                     nxt_valid = true;
@@ -752,7 +757,11 @@ template <bool SPLIT> struct PoolWalker {
     // hides behind the granules still in the ring, and a warp never holds a chunk it will not start
     // for long -- when a pool runs dry, every warp has at most the rest of one chunk left.
     __device__ __forceinline__ void claim_ahead(const GemvArgs &a, int lane) {
+#if L2D_CLAIM_EARLY
+        if (nxt_valid || pool >= 2 || row + 1 < end) return;  // with the first copy of the chunk's last row
+#else
         if (nxt_valid || pool >= 2 || mask != 0u || row + 1 < end) return;
+#endif
         if (lane == 0) nxt = atomicAdd(pool_counter(a, pool, grp), 1ull);
         nxt_valid = true;
     }
@@ -1542,10 +1551,17 @@ bool use_ring(const l2d_plan *p, bool split) {
 #ifndef L2D_WHOLE_EXTRA_PERMILLE
 #define L2D_WHOLE_EXTRA_PERMILLE 10
 #endif
+#ifndef L2D_SPLIT_CHUNK_SHARE
+#define L2D_SPLIT_CHUNK_SHARE 0  // 1: split-pool chunks sized on the group's half of each row
+#endif
+#ifndef L2D_FIRST_PER_WARP
+#define L2D_FIRST_PER_WARP 0     // 1: the first claim gives every warp a chunk when the pool has enough
+#endif
 struct RingPools {
-    int64_t whole_lo = 0;  // rows [whole_lo, rows_total) are the whole pool
-    int64_t chunk = 1;     // rows per claim
-    int first[2] = {0, 0}; // chunks of each group's CTAs' first claim (group 0's for unsplit calls)
+    int64_t whole_lo = 0;    // rows [whole_lo, rows_total) are the whole pool
+    int64_t chunk = 1;       // rows per claim from the whole pool
+    int64_t chunk_split = 1; // rows per claim from a split pool
+    int first[2] = {0, 0};   // chunks of each group's CTAs' first claim (group 0's for unsplit calls)
 };
 
 RingPools ring_pools(const l2d_plan *p, bool split, int mode) {
@@ -1553,6 +1569,11 @@ RingPools ring_pools(const l2d_plan *p, bool split, int mode) {
     const int64_t R = p->rows_total, rb = std::max<int64_t>(p->desc.N * p->eb_in, 1);
     const int64_t warps = static_cast<int64_t>(std::max(p->n_slots, 1)) * kTmaWarps;
     rp.chunk = std::max<int64_t>(1, std::min<int64_t>({16, (int64_t(32) << 10) / rb, R / (4 * warps)}));
+    rp.chunk_split = rp.chunk;
+#if L2D_SPLIT_CHUNK_SHARE
+    // A group takes about half of each split row, so twice the rows make the same bytes per claim.
+    if (split) rp.chunk_split = std::max<int64_t>(1, std::min<int64_t>({16, (int64_t(64) << 10) / rb, R / (2 * warps)}));
+#endif
     int n_ctas[2] = {p->n_slots, p->n_slots};
     if (!split) {
         rp.whole_lo = 0;
@@ -1576,9 +1597,15 @@ RingPools ring_pools(const l2d_plan *p, bool split, int mode) {
         }
     }
     const int64_t pool_rows = split ? rp.whole_lo : R;
-    const int64_t chunks = (pool_rows + rp.chunk - 1) / rp.chunk;
-    for (int g = 0; g < 2; ++g)
-        rp.first[g] = static_cast<int>(std::min<int64_t>(2 * kTmaWarps, chunks / (4 * int64_t(n_ctas[g]))));
+    const int64_t c = split ? rp.chunk_split : rp.chunk;
+    const int64_t chunks = (pool_rows + c - 1) / c;
+    for (int g = 0; g < 2; ++g) {
+        int64_t f = std::min<int64_t>(2 * kTmaWarps, chunks / (4 * int64_t(n_ctas[g])));
+#if L2D_FIRST_PER_WARP
+        f = std::max<int64_t>(f, std::min<int64_t>(kTmaWarps, chunks / (2 * int64_t(n_ctas[g]))));
+#endif
+        rp.first[g] = static_cast<int>(f);
+    }
     return rp;
 }
 
@@ -1629,6 +1656,7 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     const RingPools rp = ring_pools(p, split, mode);
     a.whole_lo = rp.whole_lo;
     a.pool_chunk = rp.chunk;
+    a.pool_chunk_split = rp.chunk_split;
     a.first_chunks[0] = rp.first[0];
     a.first_chunks[1] = rp.first[1];
     if (p->has_domains)
@@ -1653,7 +1681,8 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
 // (a call that reaches the kernel with a missing scratch pointer is refused, never launched).
 int check_args(const GemvArgs &a) {
     if (!a.x || !a.y || !a.sm_slot || !a.part || !a.meet || !a.claim || !a.ctl || a.n_slots <= 0 ||
-        (a.use_tma && (!a.xch || a.pool_chunk <= 0 || a.whole_lo < 0 || a.whole_lo > a.rows_total ||
+        (a.use_tma && (!a.xch || a.pool_chunk <= 0 || a.pool_chunk_split <= 0 || a.whole_lo < 0 ||
+                       a.whole_lo > a.rows_total ||
                        (!a.x_smem && !a.x_glob) || (a.x_glob && a.row_bytes <= 0))) ||
         (a.row_bytes > 0 && (!a.A || !a.region_base)))
         return set_error(L2D_ERR_INVALID, "gemv arguments incomplete (internal error)");

@@ -91,6 +91,22 @@ def test_binary_contract_quick(tmp_path):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("dtype,M,K", [("fp16", 4096, 4096), ("bf16", 28672, 8192), ("fp32", 4096, 4096)])
+def test_cublas_comparator_dtypes(dtype, M, K):
+    """The cuBLAS column at the new dtypes (cublasGemmEx with fp32 compute for fp16/bf16; the
+    reference's binary has only cublasSgemv, gemv_cublas_benchmark.cu:75-89): same argv and stdout
+    contract, a positive time, and the matrix size it reports matches the dtype."""
+    pytest.importorskip("torch").cuda.is_available() or pytest.skip("no GPU")
+    c = subprocess.run([os.path.join(BIN, "gemv_cublas_benchmark"), str(M), str(K), "5", "2", "0", dtype],
+                       capture_output=True, text=True, timeout=300)
+    assert c.returncode == 0, c.stderr
+    assert parse(c.stdout, "cublas_ms") > 0
+    eb = 4 if dtype == "fp32" else 2
+    assert f"matrix={M * K * eb / 2**20:.1f} MiB" in c.stdout
+    assert ("SGEMV" in c.stdout) == (dtype == "fp32")
+
+
+@pytest.mark.gpu
 def test_calibration_tools(tmp_path):
     pytest.importorskip("torch").cuda.is_available() or pytest.skip("no GPU")
     env = dict(os.environ, SIDEDGPU_CONFIG_DIR=str(tmp_path))
