@@ -58,7 +58,8 @@ enum {
     L2D_ERR_UNSUPPORTED = -7,
     L2D_ERR_IO = -8,               /* file read/write or format error */
     L2D_ERR_NCCL = -9,
-    L2D_ERR_NOT_LINEAR = -10       /* the address hash is not XOR-linear within a 2 MiB page */
+    L2D_ERR_NOT_LINEAR = -10,      /* the address hash is not XOR-linear within a 2 MiB page */
+    L2D_ERR_STALE = -11            /* a cached domain map belongs to another GPU, SM count or driver */
 };
 
 /* ---- element types and execution modes ---- */
@@ -154,6 +155,28 @@ L2D_API int l2d_read_smid2side_csv(const char *path, int *map, int cap, int *num
 L2D_API int l2d_write_mask_csv(const char *path, uint32_t mask);
 L2D_API int l2d_read_mask_csv(const char *path, uint32_t *mask);
 
+/* ---- domain-map cache (replaces utility/sidedgpu.cu:278-300 read_smid2side, :487-507 read_mask,
+ *      :118-130 the $SIDEDGPU_CONFIG_DIR lookup) ----
+ * A cache directory holds smid2side.csv and mask.csv in the reference formats plus l2d_device.txt,
+ * one line naming the device the map was probed on (l2d_device_key).  The reference trusts any
+ * smid2side.csv whose entry count equals the SM count; here a map is reused only when the key
+ * matches too, so a map probed on another GPU, after a driver update or under a different SM count
+ * is never applied.  When $SIDEDGPU_CONFIG_DIR is set, l2d_plan_create reads the cache instead of
+ * running the SM probe (l2d_plan_stats.sm_map_cached) and probes when it is missing, corrupt or
+ * stale; the calibration tools write it. */
+#define L2D_DEVICE_KEY_MAX 256
+/* "uuid=GPU-...;sm=148;cc=10.0;cuda_driver=12090;name=..." for a device. */
+L2D_API int l2d_device_key(int device, char *key, int cap);
+/* Reads the cache in dir and checks it against key (NULL: skip the identity check, as the reference
+ * does) and num_sm (0: skip).  L2D_ERR_IO: a file is missing or malformed; L2D_ERR_STALE: the key or
+ * the SM count differs, or a domain has no SM.  mask may be NULL (mask.csv then is not read). */
+L2D_API int l2d_domain_cache_check(const char *dir, const char *key, int num_sm, int *map, int cap, int *num_sm_out,
+                                   uint32_t *mask);
+/* Writes smid2side.csv, mask.csv and l2d_device.txt into dir (which must exist). */
+L2D_API int l2d_domain_cache_store(const char *dir, const char *key, const int *map, int num_sm, uint32_t mask);
+/* l2d_domain_cache_check against this device's key and SM count. */
+L2D_API int l2d_domain_cache_load(int device, const char *dir, int *map, int cap, int *num_sm, uint32_t *mask);
+
 /* ---- GEMV plans ---- */
 typedef struct l2d_plan l2d_plan;
 
@@ -205,6 +228,7 @@ typedef struct {
     int ring_modes;              /* bit m set: calls in mode m run the granule-ring kernels */
     int64_t ring_whole_rows;     /* ring calls in AWARE / OBLIVIOUS: the last rows, taken whole by either group */
     int64_t ring_chunk_rows;     /* ring calls: rows per claim from a row pool */
+    int sm_map_cached;           /* 1: the SM map was read from the domain-map cache, 0: probed or given */
 } l2d_plan_stats;
 
 /* Creates a plan.  map == NULL probes the device and desc->A's region (2 MiB pages covering

@@ -38,7 +38,8 @@ PAGE_BYTES = 2 * 1024 * 1024
 OK = 0
 STATUS_NAMES = {0: "L2D_OK", -1: "L2D_ERR_INVALID", -2: "L2D_ERR_CUDA", -3: "L2D_ERR_NO_DEVICE",
                 -4: "L2D_ERR_PROBE_TIMEOUT", -5: "L2D_ERR_PROBE_COVERAGE", -6: "L2D_ERR_PROBE_AMBIGUOUS",
-                -7: "L2D_ERR_UNSUPPORTED", -8: "L2D_ERR_IO", -9: "L2D_ERR_NCCL", -10: "L2D_ERR_NOT_LINEAR"}
+                -7: "L2D_ERR_UNSUPPORTED", -8: "L2D_ERR_IO", -9: "L2D_ERR_NCCL", -10: "L2D_ERR_NOT_LINEAR",
+                -11: "L2D_ERR_STALE"}
 
 
 class L2DError(RuntimeError):
@@ -82,7 +83,7 @@ class PlanStats(C.Structure):
                 ("split_rows", C.c_int64), ("domain_sms", C.c_int * 2), ("grid", C.c_int), ("block", C.c_int),
                 ("scratch_bytes", C.c_size_t), ("fallback_slots", C.c_uint64), ("calls", C.c_uint64),
                 ("tma", C.c_int), ("device_errors", C.c_uint64), ("ring_modes", C.c_int),
-                ("ring_whole_rows", C.c_int64), ("ring_chunk_rows", C.c_int64)]
+                ("ring_whole_rows", C.c_int64), ("ring_chunk_rows", C.c_int64), ("sm_map_cached", C.c_int)]
 
 
 # Every symbol include/l2d.h declares, with its ctypes signature.
@@ -111,6 +112,10 @@ SIGNATURES = {
     "l2d_read_smid2side_csv": (_i, [C.c_char_p, _pi, _i, _pi]),
     "l2d_write_mask_csv": (_i, [C.c_char_p, _u32]),
     "l2d_read_mask_csv": (_i, [C.c_char_p, _pu32]),
+    "l2d_device_key": (_i, [_i, C.c_char_p, _i]),
+    "l2d_domain_cache_check": (_i, [C.c_char_p, C.c_char_p, _i, _pi, _i, _pi, _pu32]),
+    "l2d_domain_cache_store": (_i, [C.c_char_p, C.c_char_p, _pi, _i, _u32]),
+    "l2d_domain_cache_load": (_i, [_i, C.c_char_p, _pi, _i, _pi, _pu32]),
     "l2d_plan_create": (_i, [C.POINTER(GemvDesc), C.POINTER(DomainMap), C.POINTER(_vp)]),
     "l2d_plan_destroy": (_i, [_vp]),
     "l2d_gemv": (_i, [_vp, _vp, _vp, _vp, _i, _vp]),
@@ -299,6 +304,43 @@ def read_mask_csv(path: str) -> int:
     m = C.c_uint32(0)
     check(lib().l2d_read_mask_csv(path.encode(), C.byref(m)))
     return int(m.value)
+
+
+# --------------------------------------------------------------------------------------------
+# Domain-map cache (utility/sidedgpu.cu:118-130, 278-300, 487-507 read the same files back)
+# --------------------------------------------------------------------------------------------
+
+def device_key(device: int = 0) -> str:
+    """The identity a cached map is keyed to: GPU UUID, SM count, compute capability, driver API."""
+    buf = C.create_string_buffer(512)
+    check(lib().l2d_device_key(device, buf, 512))
+    return buf.value.decode()
+
+
+def domain_cache_store(directory: str, key: str, sm_map: Sequence[int], mask: int) -> None:
+    arr = (C.c_int * len(sm_map))(*sm_map)
+    check(lib().l2d_domain_cache_store(directory.encode(), key.encode(), arr, len(sm_map), mask))
+
+
+def domain_cache_check(directory: str, key: Optional[str], num_sm: int = 0):
+    """(sm_map, mask) from the cache in `directory` if it belongs to `key` (None: not checked) and
+    has `num_sm` SMs (0: not checked); raises L2DError (L2D_ERR_IO / L2D_ERR_STALE) otherwise."""
+    n = C.c_int(0)
+    m = C.c_uint32(0)
+    cap = 1024
+    arr = (C.c_int * cap)()
+    check(lib().l2d_domain_cache_check(directory.encode(), key.encode() if key is not None else None, num_sm, arr,
+                                       cap, C.byref(n), C.byref(m)))
+    return list(arr[: n.value]), int(m.value)
+
+
+def domain_cache_load(directory: str, device: int = 0):
+    """domain_cache_check against this device's key and SM count."""
+    n = C.c_int(0)
+    m = C.c_uint32(0)
+    arr = (C.c_int * 1024)()
+    check(lib().l2d_domain_cache_load(device, directory.encode(), arr, 1024, C.byref(n), C.byref(m)))
+    return list(arr[: n.value]), int(m.value)
 
 
 # --------------------------------------------------------------------------------------------

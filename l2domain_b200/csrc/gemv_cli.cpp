@@ -136,10 +136,9 @@ int main(int argc, char **argv) {
     CLI_L2D(l2d_plan_domain_map(plan, sm_map.data(), num_sm, &num_sm, &mask));
     if (const char *dir = std::getenv("SIDEDGPU_CONFIG_DIR")) {
         if (dir[0]) {
-            std::string d(dir);
-            if (d.back() != '/') d += '/';
-            CLI_L2D(l2d_write_smid2side_csv((d + "smid2side.csv").c_str(), sm_map.data(), num_sm));
-            CLI_L2D(l2d_write_mask_csv((d + "mask.csv").c_str(), mask));
+            char key[L2D_DEVICE_KEY_MAX + 1];
+            CLI_L2D(l2d_device_key(device, key, sizeof key));
+            CLI_L2D(l2d_domain_cache_store(dir, key, sm_map.data(), num_sm, mask));
         }
     }
     // Row-start placement counts, as the reference prints them (side of each row's first byte).

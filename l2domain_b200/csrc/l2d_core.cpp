@@ -49,6 +49,7 @@ const char *l2d_status_string(int status) {
     case L2D_ERR_IO: return "I/O or format error";
     case L2D_ERR_NCCL: return "NCCL error";
     case L2D_ERR_NOT_LINEAR: return "address hash is not XOR-linear within a page";
+    case L2D_ERR_STALE: return "cached domain map belongs to another device or driver";
     default: return "unknown status";
     }
 }
@@ -387,6 +388,73 @@ int l2d_analyze_addr(size_t n, const uint64_t *offsets, const uint32_t *lat, con
         return set_error(L2D_ERR_NOT_LINEAR, "linear model (mask 0x%08x) predicts only %.3f of validation lines", mask,
                          magree);
     if (worst < 0.75) return set_error(L2D_ERR_PROBE_AMBIGUOUS, "a page's attr votes agree only %.2f", worst);
+    return L2D_OK;
+}
+
+// ---- domain-map cache ----------------------------------------------------------------------
+
+}  // extern "C"
+
+namespace {
+
+std::string cache_path(const char *dir, const char *file) {
+    std::string p(dir);
+    if (!p.empty() && p.back() != '/') p += '/';
+    return p + file;
+}
+
+}  // namespace
+
+extern "C" {
+
+int l2d_domain_cache_check(const char *dir, const char *key, int num_sm, int *map, int cap, int *num_sm_out,
+                           uint32_t *mask) {
+    if (!dir || !dir[0] || !num_sm_out) return set_error(L2D_ERR_INVALID, "domain_cache_check: bad arguments");
+    if (key) {
+        const std::string path = cache_path(dir, "l2d_device.txt");
+        FILE *f = std::fopen(path.c_str(), "r");
+        if (!f) return set_error(L2D_ERR_STALE, "'%s' missing: the map's device is unknown", path.c_str());
+        char buf[L2D_DEVICE_KEY_MAX + 2] = {0};
+        const size_t n = std::fread(buf, 1, sizeof buf - 1, f);
+        std::fclose(f);
+        std::string got(buf, n);
+        while (!got.empty() && (got.back() == '\n' || got.back() == '\r')) got.pop_back();
+        if (got != key) return set_error(L2D_ERR_STALE, "cache key '%s' differs from this device '%s'", got.c_str(), key);
+    }
+    int n = 0;
+    int st = l2d_read_smid2side_csv(cache_path(dir, "smid2side.csv").c_str(), nullptr, 0, &n);
+    if (st != L2D_OK) return st;
+    if (num_sm > 0 && n != num_sm)
+        return set_error(L2D_ERR_STALE, "cached map has %d SMs, the device has %d", n, num_sm);
+    std::vector<int> m(n);
+    st = l2d_read_smid2side_csv(cache_path(dir, "smid2side.csv").c_str(), m.data(), n, &n);
+    if (st != L2D_OK) return st;
+    const int ones = static_cast<int>(std::count(m.begin(), m.end(), 1));
+    if (ones == 0 || ones == n) return set_error(L2D_ERR_STALE, "cached map puts every SM in one domain");
+    if (mask) {
+        st = l2d_read_mask_csv(cache_path(dir, "mask.csv").c_str(), mask);
+        if (st != L2D_OK) return st;
+    }
+    *num_sm_out = n;
+    if (map) {
+        if (cap < n) return set_error(L2D_ERR_INVALID, "capacity %d < %d SMs", cap, n);
+        std::copy(m.begin(), m.end(), map);
+    }
+    return L2D_OK;
+}
+
+int l2d_domain_cache_store(const char *dir, const char *key, const int *map, int num_sm, uint32_t mask) {
+    if (!dir || !dir[0] || !key || !map || num_sm <= 0)
+        return set_error(L2D_ERR_INVALID, "domain_cache_store: bad arguments");
+    if (std::strlen(key) > L2D_DEVICE_KEY_MAX) return set_error(L2D_ERR_INVALID, "device key too long");
+    int st = l2d_write_smid2side_csv(cache_path(dir, "smid2side.csv").c_str(), map, num_sm);
+    if (st == L2D_OK) st = l2d_write_mask_csv(cache_path(dir, "mask.csv").c_str(), mask);
+    if (st != L2D_OK) return st;
+    const std::string path = cache_path(dir, "l2d_device.txt");
+    FILE *f = std::fopen(path.c_str(), "w");
+    if (!f) return set_error(L2D_ERR_IO, "cannot open '%s': %s", path.c_str(), std::strerror(errno));
+    std::fprintf(f, "%s\n", key);
+    if (std::fclose(f) != 0) return set_error(L2D_ERR_IO, "cannot close '%s'", path.c_str());
     return L2D_OK;
 }
 

@@ -577,27 +577,47 @@ __device__ __forceinline__ void run_slot(const GemvArgs &a, int slot, int warp, 
     }
 }
 
-// Sharded prologue, the whole CTA (batch 1, x staged once for all of the CTA's slots).
-//  Rank 0: CTA b stores its share of x's 4-byte words into every peer's flagged-word buffer as
-//  (word, step) pairs, 8-byte stores that arrive whole, then stages its own x.
-//  Other ranks: read their flagged-word buffer 16 bytes (two words) at a time until both flags
-//  carry this step (bounded by the timeout; status bit 0 when it runs out) and stage the words.
+// Rank 0 of a sharded ring call, the whole CTA, first thing after the launch: this CTA's share of
+// x's words into every peer's flagged-word buffer, two words per 16-byte store {w0, step, w1, step}
+// (each 8-byte half arrives whole, and the reader checks both flags).  The peers start streaming A
+// as soon as their x words land, so the push comes before rank 0's own pool claim and copies.
+// Threads [t0, blockDim.x) take part (the ring kernels leave warp 0 free for the pool claim).
+__device__ __forceinline__ void shard_push_x(const GemvArgs &a, int t0) {
+    const int64_t words = (a.x_bytes + 3) / 4, pairs = (words + 1) / 2;
+    const int64_t lo = pairs * blockIdx.x / gridDim.x, hi = pairs * (blockIdx.x + 1) / gridDim.x;
+    const uint32_t flag = static_cast<uint32_t>(a.shard_epoch);
+    const uint32_t *xw = reinterpret_cast<const uint32_t *>(a.x);
+    if (static_cast<int>(threadIdx.x) < t0) return;
+    for (int64_t j = lo + threadIdx.x - t0; j < hi; j += blockDim.x - t0) {
+        const uint32_t v0 = xw[2 * j], v1 = 2 * j + 1 < words ? xw[2 * j + 1] : 0u;
+        for (int p = 1; p < a.shard_world; ++p)
+            asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(a.peer_xw[p] + 2 * j), "r"(v0),
+                         "r"(flag), "r"(v1), "r"(flag)
+                         : "memory");
+    }
+}
+
+// Sharded prologue of the register kernels, the whole CTA (batch 1, x staged once for all of the
+// CTA's slots).
+//  Rank 0: pushes this CTA's share of x (shard_push_x), then stages its own x.
+//  Other ranks (shard_wait_x, which the ring kernels call once their first copies are in flight):
+//  read their flagged-word buffer 16 bytes (two words) at a time until both flags carry this step
+//  (bounded by the timeout; status bit 0 when it runs out) and stage the words.
+__device__ __forceinline__ void shard_wait_x(const GemvArgs &a, uint8_t *smem);
+
 template <bool SH> __device__ __forceinline__ void shard_stage_x(const GemvArgs &a, uint8_t *smem) {
     if (!SH) return;
-    const int64_t words = (a.x_bytes + 3) / 4;
-    const uint32_t flag = static_cast<uint32_t>(a.shard_epoch);
     if (a.shard_rank == 0) {
-        const int64_t lo = words * blockIdx.x / gridDim.x, hi = words * (blockIdx.x + 1) / gridDim.x;
-        const uint32_t *xw = reinterpret_cast<const uint32_t *>(a.x);
-        for (int64_t w = lo + threadIdx.x; w < hi; w += blockDim.x) {
-            const uint32_t v = xw[w];
-            for (int p = 1; p < a.shard_world; ++p)
-                asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(a.peer_xw[p] + w), "r"(v), "r"(flag)
-                             : "memory");
-        }
+        shard_push_x(a, 0);
         stage_x(a, smem, 0, 1);
         return;
     }
+    shard_wait_x(a, smem);
+}
+
+__device__ __forceinline__ void shard_wait_x(const GemvArgs &a, uint8_t *smem) {
+    const int64_t words = (a.x_bytes + 3) / 4;
+    const uint32_t flag = static_cast<uint32_t>(a.shard_epoch);
     const uint2 *xw = a.peer_xw[a.shard_rank];
     uint32_t *dst = reinterpret_cast<uint32_t *>(smem);
     const uint64_t deadline = dev::globaltimer_ns() + a.shard_timeout_ns;
@@ -861,8 +881,8 @@ __device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long
     }
     __syncwarp();
     if (stage_x_now) {
-        if (SH) {
-            shard_stage_x<SH>(a, smem);
+        if (SH && a.shard_rank != 0) {
+            shard_wait_x(a, smem);  // rank 0 pushed x at the start and staged its own like an unsharded call
         } else {
             asm volatile("cp.async.wait_all;" ::: "memory");
             __syncthreads();
@@ -996,9 +1016,10 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
         SPLIT && sm < static_cast<uint32_t>(kMaxSmid) ? static_cast<int>((a.grp_bits[sm >> 5] >> (sm & 31)) & 1u) : 0;
     const unsigned long long epoch = ld_claim(a.ctl + kCtlEpoch) + 1ull;
     const int first = a.first_chunks[grp];
+    if (SH && a.shard_rank == 0) shard_push_x(a, 32);  // the peers wait for x: it goes out first
     if (tid == 0 && first > 0)
         s_k0 = static_cast<long long>(atomicAdd(pool_counter(a, SPLIT ? 0 : 1, grp), static_cast<unsigned long long>(first)));
-    if (!SH && !a.x_glob) stage_x_issue(a, smem);
+    if ((!SH || a.shard_rank == 0) && !a.x_glob) stage_x_issue(a, smem);
     // The attr words reach L1 while the first claim is in flight: the first ballot of every warp
     // reads them before its first copy can start.
     if (SPLIT && a.dom_kind == 0 && tid < (a.attr_words + 31) / 32)
@@ -1174,29 +1195,48 @@ int probe_addr_domains_impl(int device, const uint8_t *base, size_t valid_bytes,
 namespace {
 
 std::mutex g_sm_cache_mu;
-std::map<int, std::vector<int>> g_sm_cache;  // device -> SM domain map
+std::map<int, std::pair<std::vector<int>, bool>> g_sm_cache;  // device -> (SM domain map, read from the cache files)
 
 }  // namespace
 
-// SM -> domain map of a device, probed once per process.
-int cached_sm_map(int device, std::vector<int> &out) {
+// SM -> domain map of a device, once per process: read from the domain-map cache in
+// $SIDEDGPU_CONFIG_DIR when that holds a map keyed to this device (utility/sidedgpu.cu:118-130,
+// 278-300 read it from the same place), probed otherwise.  *from_file tells which.
+int cached_sm_map(int device, std::vector<int> &out, bool *from_file) {
     {
         std::lock_guard<std::mutex> lk(g_sm_cache_mu);
         auto it = g_sm_cache.find(device);
         if (it != g_sm_cache.end()) {
-            out = it->second;
+            out = it->second.first;
+            if (from_file) *from_file = it->second.second;
             return L2D_OK;
         }
     }
-    int n = 0;
-    int st = probe_sm_domains_impl(device, nullptr, 0, &n, nullptr, nullptr, nullptr, 0, nullptr);
-    if (st != L2D_OK) return st;
-    std::vector<int> map(n, 0);
-    st = probe_sm_domains_impl(device, map.data(), n, &n, nullptr, nullptr, nullptr, 0, nullptr);
-    if (st != L2D_OK) return st;
+    std::vector<int> map;
+    bool file = false;
+    const char *dir = std::getenv("SIDEDGPU_CONFIG_DIR");
+    if (dir && dir[0]) {
+        int n = 0;
+        std::vector<int> m(kMaxSmid, 0);
+        if (l2d_domain_cache_load(device, dir, m.data(), kMaxSmid, &n, nullptr) == L2D_OK) {
+            m.resize(n);
+            map = m;
+            file = true;
+        }
+        clear_error();  // a missing or stale cache is not an error: the probe runs instead
+    }
+    if (!file) {
+        int n = 0;
+        int st = probe_sm_domains_impl(device, nullptr, 0, &n, nullptr, nullptr, nullptr, 0, nullptr);
+        if (st != L2D_OK) return st;
+        map.assign(n, 0);
+        st = probe_sm_domains_impl(device, map.data(), n, &n, nullptr, nullptr, nullptr, 0, nullptr);
+        if (st != L2D_OK) return st;
+    }
     std::lock_guard<std::mutex> lk(g_sm_cache_mu);
-    g_sm_cache[device] = map;
+    g_sm_cache[device] = std::make_pair(map, file);
     out = map;
+    if (from_file) *from_file = file;
     return L2D_OK;
 }
 
@@ -1256,6 +1296,7 @@ struct l2d_plan {
     bool tma_force = false;   // L2D_PLAN_TMA: use them for every mode
     size_t ring_off = 0;      // their ring block's offset in dynamic shared memory
     bool ring_xglob = false;  // batched ring calls: x read from global memory per problem
+    bool sm_map_cached = false;  // the SM map came from the domain-map cache files, not a probe
     unsigned long long *d_claim = nullptr;
     unsigned long long *d_ctl = nullptr;
 };
@@ -1369,7 +1410,7 @@ int l2d_plan_create(const l2d_gemv_desc *desc_in, const l2d_domain_map *map, l2d
         p->attr.assign(map->attr, map->attr + map->num_pages);
         p->has_domains = true;
     } else if (span > 0 && !(d.flags & L2D_PLAN_NO_PROBE)) {
-        st = cached_sm_map(d.device, p->sm_domain);
+        st = cached_sm_map(d.device, p->sm_domain, &p->sm_map_cached);
         if (st != L2D_OK) {
             delete p;
             return st;
@@ -1784,6 +1825,7 @@ int l2d_plan_stats_get(l2d_plan *p, l2d_plan_stats *s) {
         s->ring_whole_rows = p->rows_total - rp.whole_lo;
     }
     s->scratch_bytes = p->dev_bytes;
+    s->sm_map_cached = p->sm_map_cached ? 1 : 0;
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(p->device);

@@ -284,6 +284,35 @@ int l2d_read_stream(int device, const void *p, size_t bytes, uint32_t *sink, siz
     return L2D_OK;
 }
 
+int l2d_device_key(int device, char *key, int cap) {
+    clear_error();
+    if (!key || cap <= 0) return set_error(L2D_ERR_INVALID, "device_key: bad arguments");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return set_error(L2D_ERR_NO_DEVICE, "no CUDA device");
+    if (device < 0 || device >= ndev) return set_error(L2D_ERR_INVALID, "device %d out of range", device);
+    cudaDeviceProp prop;
+    L2D_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    int drv = 0;
+    L2D_CUDA_TRY(cudaDriverGetVersion(&drv));
+    const unsigned char *u = reinterpret_cast<const unsigned char *>(prop.uuid.bytes);
+    char uuid[48];
+    std::snprintf(uuid, sizeof uuid, "GPU-%02x%02x%02x%02x-%02x%02x-%02x%02x-%02x%02x-%02x%02x%02x%02x%02x%02x", u[0], u[1],
+                  u[2], u[3], u[4], u[5], u[6], u[7], u[8], u[9], u[10], u[11], u[12], u[13], u[14], u[15]);
+    const int n = std::snprintf(key, static_cast<size_t>(cap), "uuid=%s;sm=%d;cc=%d.%d;cuda_driver=%d;name=%s", uuid,
+                                prop.multiProcessorCount, prop.major, prop.minor, drv, prop.name);
+    if (n < 0 || n >= cap) return set_error(L2D_ERR_INVALID, "device_key: capacity %d too small", cap);
+    return L2D_OK;
+}
+
+int l2d_domain_cache_load(int device, const char *dir, int *map, int cap, int *num_sm, uint32_t *mask) {
+    char key[L2D_DEVICE_KEY_MAX + 1];
+    int st = l2d_device_key(device, key, sizeof key);
+    if (st != L2D_OK) return st;
+    int n = 0;
+    L2D_CUDA_TRY(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
+    return l2d_domain_cache_check(dir, key, n, map, cap, num_sm, mask);
+}
+
 int l2d_device_info(int device, int *num_sm, int *l2_bytes, int *cc_major, int *cc_minor, char *name, int name_cap) {
     clear_error();
     int ndev = 0;

@@ -33,8 +33,9 @@ inline int parity_domain(uint32_t mask, uint64_t addr, int attr) {
 
 inline int lowest_bit_or(uint32_t mask, int fallback) { return mask ? __builtin_ctz(mask) : fallback; }
 
-// SM -> domain map of a device, probed once per process (l2d_gemv.cu).
-int cached_sm_map(int device, std::vector<int> &out);
+// SM -> domain map of a device, once per process: read from the domain-map cache when
+// $SIDEDGPU_CONFIG_DIR holds one keyed to the device, probed otherwise (l2d_gemv.cu).
+int cached_sm_map(int device, std::vector<int> &out, bool *from_file = nullptr);
 
 // Peer-memory sharding fields of one l2d_gemv_sharded step (device pointers unless noted).
 struct ShardArgs {

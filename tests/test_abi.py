@@ -93,6 +93,67 @@ def test_missing_files_are_io_errors(tmp_path):
 
 
 # ---------------------------------------------------------------------------------------------
+# Domain-map cache: reused only for the device it was probed on
+# ---------------------------------------------------------------------------------------------
+
+KEY = "uuid=GPU-00000000-1111-2222-3333-444444444444;sm=148;cc=10.0;cuda_driver=12090;name=NVIDIA B200"
+SM_MAP = [(s // 2) % 2 for s in range(148)]
+
+
+def test_domain_cache_roundtrip_keeps_reference_formats(tmp_path):
+    L.domain_cache_store(str(tmp_path), KEY, SM_MAP, 0x1EF000)
+    assert L.domain_cache_check(str(tmp_path), KEY, 148) == (SM_MAP, 0x1EF000)
+    # The files are the reference's formats: its tools and readers take them as they are.
+    assert open(tmp_path / "smid2side.csv").read() == "".join(f"{v}," for v in SM_MAP) + "\n"
+    assert open(tmp_path / "mask.csv").read() == "0x001ef000\n"
+    assert L.read_smid2side_csv(str(tmp_path / "smid2side.csv")) == SM_MAP
+
+
+@pytest.mark.parametrize("key,num_sm", [(KEY.replace("44444444", "55555555"), 148),  # another GPU
+                                        (KEY.replace("12090", "12080"), 148),         # another driver
+                                        (KEY, 132)])                                  # another SM count
+def test_domain_cache_stale_maps_are_refused(tmp_path, key, num_sm):
+    L.domain_cache_store(str(tmp_path), KEY, SM_MAP, 0x1EF000)
+    with pytest.raises(L.L2DError) as e:
+        L.domain_cache_check(str(tmp_path), key, num_sm)
+    assert e.value.status == -11
+
+
+def test_domain_cache_without_device_file(tmp_path):
+    """Files written by the reference's own tools carry no device key: refused when a key is
+    required (as the plans require), read as the reference reads them when it is not."""
+    L.write_smid2side_csv(str(tmp_path / "smid2side.csv"), SM_MAP)
+    L.write_mask_csv(str(tmp_path / "mask.csv"), 0xB3000)
+    with pytest.raises(L.L2DError) as e:
+        L.domain_cache_check(str(tmp_path), KEY, 148)
+    assert e.value.status == -11
+    assert L.domain_cache_check(str(tmp_path), None, 148) == (SM_MAP, 0xB3000)
+
+
+@pytest.mark.parametrize("what,content,status", [
+    ("smid2side.csv", "0,1,2,\n", -8),          # not a side
+    ("smid2side.csv", "", -8),                  # empty
+    ("smid2side.csv", "1," * 148 + "\n", -11),  # every SM in one domain
+    ("mask.csv", "b3000\n", -8),                # not 0x%08x
+])
+def test_domain_cache_corrupt_files_are_refused(tmp_path, what, content, status):
+    L.domain_cache_store(str(tmp_path), KEY, SM_MAP, 0x1EF000)
+    (tmp_path / what).write_text(content)
+    with pytest.raises(L.L2DError) as e:
+        L.domain_cache_check(str(tmp_path), KEY, 148)
+    assert e.value.status == status
+
+
+def test_domain_cache_load_without_gpu_reports_no_device(tmp_path):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("has a GPU")
+    arr = (C.c_int * 1024)()
+    n, m = C.c_int(0), C.c_uint32(0)
+    assert L.lib().l2d_domain_cache_load(0, str(tmp_path).encode(), arr, 1024, C.byref(n), C.byref(m)) == -3
+
+
+# ---------------------------------------------------------------------------------------------
 # Probe analysis
 # ---------------------------------------------------------------------------------------------
 

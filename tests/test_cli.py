@@ -1,6 +1,7 @@
 """The run.sh drop-in and its binaries: CPU-side option handling and dry runs, plus (GPU) the
 process contract the reference's runner parses (applications/gemv/run.sh:62-98)."""
 import csv
+import json
 import os
 import subprocess
 
@@ -115,6 +116,54 @@ def test_calibration_tools(tmp_path):
     b = subprocess.run([os.path.join(BIN, "get_mask")], capture_output=True, text=True, env=env, timeout=120)
     assert b.returncode == 0, b.stderr
     assert "mask = 0x" in b.stdout
+
+
+PLAN_Y = r"""
+import sys, json, torch
+sys.path.insert(0, {repo!r})
+import l2domain_b200 as L
+torch.cuda.set_device(0)
+M, N = 2048, 8192
+raw = torch.empty(M * N * 2 + (2 << 20), dtype=torch.uint8, device="cuda")
+off = (-raw.data_ptr()) % (2 << 20)
+A = raw[off: off + M * N * 2]
+L.fill_cfg(A, L.F16, M * N, 4, 0, 1, 0.0, 0.02)
+x = torch.empty(N * 2, dtype=torch.uint8, device="cuda")
+L.fill_cfg(x, L.F16, N, 4, 1, 1, 0.0, 1.0)
+y = torch.empty(M * 2, dtype=torch.uint8, device="cuda")
+plan = L.GemvPlan(A, M, N, L.F16, L.F16)
+plan.gemv(A, x, y, L.MODE_AWARE)
+torch.cuda.synchronize()
+print(json.dumps({{"cached": plan.stats()["sm_map_cached"], "y": y.cpu().tolist()[:4096:7]}}))
+"""
+
+
+@pytest.mark.gpu
+def test_domain_map_cache_reused_by_plans(tmp_path):
+    """get_smid2side writes the map with its device key; --validate re-probes and agrees; a plan made
+    in a fresh process with SIDEDGPU_CONFIG_DIR set reads the map instead of probing and gives the
+    same bits as a probed plan; a cache keyed to another device is not used (the plan probes) and
+    --validate reports it."""
+    pytest.importorskip("torch").cuda.is_available() or pytest.skip("no GPU")
+    env = dict(os.environ, SIDEDGPU_CONFIG_DIR=str(tmp_path))
+    a = subprocess.run([os.path.join(BIN, "get_smid2side")], capture_output=True, text=True, env=env, timeout=120)
+    assert a.returncode == 0, a.stderr
+    assert (tmp_path / "l2d_device.txt").read_text().startswith("uuid=GPU-")
+    v = subprocess.run([os.path.join(BIN, "get_smid2side"), "--validate"], capture_output=True, text=True, env=env,
+                       timeout=120)
+    assert v.returncode == 0 and "0 of" in v.stdout, v.stdout + v.stderr
+    code = PLAN_Y.format(repo=REPO)
+    run = lambda e: json.loads(subprocess.run(["python3", "-c", code], capture_output=True, text=True, env=e,
+                                              timeout=300, check=True).stdout.strip().splitlines()[-1])
+    plain = {k: v for k, v in os.environ.items() if k != "SIDEDGPU_CONFIG_DIR"}
+    cached, probed = run(env), run(plain)
+    assert cached["cached"] == 1 and probed["cached"] == 0
+    assert cached["y"] == probed["y"]
+    (tmp_path / "l2d_device.txt").write_text("uuid=GPU-another;sm=148\n")
+    assert run(env)["cached"] == 0
+    v = subprocess.run([os.path.join(BIN, "get_smid2side"), "--validate"], capture_output=True, text=True, env=env,
+                       timeout=120)
+    assert v.returncode == 4
 
 
 @pytest.mark.gpu
