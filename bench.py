@@ -313,6 +313,15 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
     def gbs(nbytes, us):
         return {k: round(nbytes / (v * 1e-6) / 1e9, 1) for k, v in us.items() if v}
 
+    def sided_us(A, x, y, M, N, dt, calls):
+        """The same matrix packed by L2 domain (l2d_sided_*): µs per call of each mode."""
+        s = L.SidedMatrix(M, N, dt, dt, device=local)
+        s.pack(A, stream=stream)
+        res = {name: round(kernel_time_us(lambda m=mode: s.gemv(x, y, m, stream), calls, stream), 3)
+               for name, mode in (("aware", 1), ("swapped", 2), ("stream", 3))}
+        s.close()
+        return res
+
     def read_gbs(buf, nbytes, calls):
         nb = nbytes // 32 * 32
         return round(nb / (kernel_time_us(lambda: L.read_stream(buf, nb, sink, 4096, local, stream), calls, stream)
@@ -326,11 +335,16 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
     us = per_mode(plan, A, x, y, 1000)
     A2, xv, yv = A.view(tdt[dt]).view(M, N), x.view(tdt[dt]), y.view(tdt[dt])
     us["cublas_torch_mv"] = round(kernel_time_us(lambda: torch.mv(A2, xv, out=yv), 1000, stream), 3)
+    ps = L.GemvPlan(A, M, N, dt, dt, device=local, static_a=True)  # A written once: copies start early
+    for name, mode in (("aware", 1), ("stream", 3)):
+        us[f"{name}_static_a"] = round(kernel_time_us(lambda m=mode: ps.gemv(A, x, y, m, stream), 1000, stream), 3)
+    ps.close()
     g = gbs(nbytes, us)
     out["cfg2"] = {"workload": "fp16 4096x4096 (32 MiB), 1000 back-to-back calls, no flush (L2-resident)",
                    "bound": "l2", "us": us, "gbs": g, "l2_read_peak_gbs": l2_peak,
                    "frac_of_l2_read_peak": {k: round(v / l2_peak, 4) for k, v in g.items()},
-                   "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 200, 20, 0)}
+                   "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 200, 20, 0),
+                   "sided_us": sided_us(A, x, y, M, N, dt, 1000)}
     plan.close()
     del raw, A
 
@@ -344,7 +358,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                         "us": us, "gbs": g, "read_stream_gbs": read_gbs(A, M * N * 2, 500),
                         "aware_speedup_vs_stream": round(us["stream"] / us["aware"], 4),
                         "aware_speedup_vs_oblivious": round(us["oblivious"] / us["aware"], 4),
-                        "swapped_slowdown_vs_aware": round(us["swapped"] / us["aware"], 4)}
+                        "swapped_slowdown_vs_aware": round(us["swapped"] / us["aware"], 4),
+                        "sided_us": sided_us(A, x, y, M, N, dt, 500)}
     plan.close()
     del raw, A
 
@@ -384,7 +399,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                    "bound": "hbm", "us": us, "gbs": g,
                    "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in g.items()} if read_peak else None,
                    "frac_of_copy_peak": {k: round(v / copy_peak, 4) for k, v in g.items()},
-                   "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 20, 5, 0)}
+                   "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 20, 5, 0),
+                   "sided_us": sided_us(A, x, y, M, N, dt, 50)}
     plan.close()
     del raw, A
 
@@ -593,6 +609,10 @@ def run_ours(args, rank, world, local):
             out = torch.empty(m_loc, dtype=tdt, device=dev)
             A2 = A.view(tdt).view(m_loc, N)
             modes_us["cublas_torch_mv"] = round(kernel_time(lambda: torch.mv(A2, xv, out=out), args.steps), 3)
+        ps = L.GemvPlan(A, m_loc, N, dt, dt, batch=batch, device=local, static_a=True)
+        modes_us["aware_static_a"] = round(kernel_time(lambda: ps.gemv(A, x, y_loc, L.MODE_AWARE, stream),
+                                                       args.steps), 3)
+        ps.close()
         Ai = A.view(torch.int64)
         modes_us["torch_sum_read"] = round(kernel_time(lambda: torch.sum(Ai), max(5, args.steps // 5)), 3)
 

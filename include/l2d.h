@@ -201,7 +201,12 @@ enum {
                               shared-memory rings) for every mode when the shape allows them (rows on
                               4 KiB boundaries, x in shared memory); by default the plan picks them
                               per call where they were measured faster */
-    L2D_PLAN_NO_TMA = 4    /* never use the granule-ring kernels */
+    L2D_PLAN_NO_TMA = 4,   /* never use the granule-ring kernels */
+    L2D_PLAN_STATIC_A = 8  /* the caller guarantees that A is never written by the kernel launched on the
+                              stream immediately before a call (weights written once, then read by
+                              many calls): a ring call then starts copying A while the previous
+                              GEMV on the stream drains, instead of after it completes.  x and y are
+                              touched only after the previous kernel completed, either way. */
 };
 
 typedef struct {
@@ -260,6 +265,38 @@ L2D_API int l2d_plan_domain_map(const l2d_plan *plan, int *sm_domain, int cap, i
 #define L2D_NOALLOC_MAX_PAGES 32768  /* 2 MiB pages spanned by the domain map (64 GiB of A) */
 L2D_API int l2d_gemv_noalloc(const l2d_gemv_desc *desc, const l2d_domain_map *map, const void *x, void *y,
                              int mode, void *stream);
+
+/* ---- sided matrices: the domain-classified placement of utility/sidedgpu.cu:791-838 (cudaMallocSided,
+ *      which hands out 4 KiB granules homed in one L2 domain) applied to the GEMV's A ----
+ * A dense row-major M x N matrix is packed once (l2d_sided_pack) into a buffer the object owns, where
+ * rows [0, rows_side[0]) sit only in granules homed in L2 domain 0 and the other rows only in
+ * granules homed in domain 1: contiguous row ranges per domain instead of index lists.  The buffer is
+ * as large as A (every granule is used; each side takes one granule of every 8 KiB pair, which the
+ * address hash always splits between the domains).  l2d_gemv_sided computes y = A.x from it: AWARE
+ * streams each domain's rows on that domain's SMs -- whole rows, near granules only, no per-row
+ * partials -- and a group that finishes first takes over the other side's remaining rows; SWAPPED
+ * starts every group on the far side (the control); STREAM (and OBLIVIOUS, the same for whole rows)
+ * hands rows to any SM.  Every mode computes each row in one warp with its granules in order, so
+ * all modes give the same bits, equal to l2d_gemv's STREAM on the dense A.  Rows must be whole 4 KiB
+ * granules, at most 96 KiB (x is staged in shared memory); one problem. */
+typedef struct l2d_sided l2d_sided;
+typedef struct {
+    int64_t rows_side[2];   /* rows stored in domain-0 and domain-1 granules */
+    int granules_per_row;
+    const void *base;       /* the packed buffer (2 MiB aligned) */
+    size_t bytes;
+    uint32_t mask;          /* the address hash the layout follows */
+} l2d_sided_info_t;
+/* desc: M, N, dtype_in, dtype_out, device (lda, strides, A and flags are ignored; batch <= 1).
+ * Allocates the buffer and probes its pages' domains (and the SM map unless it is cached). */
+L2D_API int l2d_sided_create(const l2d_gemv_desc *desc, l2d_sided **out);
+/* Copies the dense row-major A (lda elements per row, 0 = N) into the sided layout, stream-ordered. */
+L2D_API int l2d_sided_pack(l2d_sided *s, const void *A, int64_t lda, void *stream);
+L2D_API int l2d_gemv_sided(l2d_sided *s, const void *x, void *y, int mode, void *stream);
+L2D_API int l2d_sided_info(const l2d_sided *s, l2d_sided_info_t *info);
+/* Device addresses of the granules holding row `row` (granules_per_row entries, in row order). */
+L2D_API int l2d_sided_row_granules(const l2d_sided *s, int64_t row, uint64_t *addr, int cap, int *n);
+L2D_API int l2d_sided_destroy(l2d_sided *s);
 
 /* ---- row-sharded GEMV over the GPUs of one node (peer memory; no counterpart in the reference) ----
  * One process (or one shard object) per GPU.  Rank r owns rows [row0, row0 + rows) of an M_total-row

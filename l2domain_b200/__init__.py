@@ -33,6 +33,7 @@ MODES = {"oblivious": MODE_OBLIVIOUS, "baseline": MODE_OBLIVIOUS, "aware": MODE_
 PLAN_NO_PROBE = 1
 PLAN_TMA = 2      # granule-ring kernels for every mode (when the shape allows them)
 PLAN_NO_TMA = 4   # register kernels only; default: picked per call
+PLAN_STATIC_A = 8  # A is never written by the kernel right before a call: ring calls copy A early
 PAGE_BYTES = 2 * 1024 * 1024
 
 OK = 0
@@ -122,6 +123,12 @@ SIGNATURES = {
     "l2d_plan_stats_get": (_i, [_vp, C.POINTER(PlanStats)]),
     "l2d_plan_domain_map": (_i, [_vp, _pi, _i, _pi, _pu32]),
     "l2d_gemv_noalloc": (_i, [C.POINTER(GemvDesc), C.POINTER(DomainMap), _vp, _vp, _i, _vp]),
+    "l2d_sided_create": (_i, [C.POINTER(GemvDesc), C.POINTER(_vp)]),
+    "l2d_sided_pack": (_i, [_vp, _vp, _i64, _vp]),
+    "l2d_gemv_sided": (_i, [_vp, _vp, _vp, _i, _vp]),
+    "l2d_sided_info": (_i, [_vp, _vp]),
+    "l2d_sided_row_granules": (_i, [_vp, _i64, _pu64, _i, _pi]),
+    "l2d_sided_destroy": (_i, [_vp]),
     "l2d_shard_create": (_i, [_i, _i, _i, _i64, _i64, _i64, _i64, _i, _i, _u32, C.POINTER(_vp)]),
     "l2d_shard_handle": (_i, [_vp, _vp, _sz, _psz]),
     "l2d_shard_connect": (_i, [_vp, _vp, _sz]),
@@ -363,13 +370,15 @@ class GemvPlan:
 
     def __init__(self, A, M: int, N: int, dtype_in: int = F32, dtype_out: Optional[int] = None, lda: int = 0,
                  batch: int = 1, stride_a: int = 0, stride_x: int = 0, stride_y: int = 0, device: int = 0,
-                 domains: Optional[DomainModel] = None, probe: bool = True, tma: Optional[bool] = None):
+                 domains: Optional[DomainModel] = None, probe: bool = True, tma: Optional[bool] = None,
+                 static_a: bool = False):
         self._plan = C.c_void_p(0)
         self.desc = GemvDesc(M=M, N=N, lda=lda, dtype_in=dtype_in,
                              dtype_out=dtype_in if dtype_out is None else dtype_out, batch=batch,
                              stride_a=stride_a, stride_x=stride_x, stride_y=stride_y, device=device,
                              A=_ptr(A), flags=(0 if probe else PLAN_NO_PROBE) |
-                             (0 if tma is None else PLAN_TMA if tma else PLAN_NO_TMA))
+                             (0 if tma is None else PLAN_TMA if tma else PLAN_NO_TMA) |
+                             (PLAN_STATIC_A if static_a else 0))
         dm = None
         if domains is not None:
             self._sm = (C.c_int * len(domains.sm_domain))(*domains.sm_domain)
@@ -400,6 +409,57 @@ class GemvPlan:
         if self._plan and self._plan.value:
             check(lib().l2d_plan_destroy(self._plan))
             self._plan = C.c_void_p(0)
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class SidedInfo(C.Structure):
+    _fields_ = [("rows_side", C.c_int64 * 2), ("granules_per_row", C.c_int), ("base", C.c_void_p),
+                ("bytes", C.c_size_t), ("mask", C.c_uint32)]
+
+
+class SidedMatrix:
+    """A copy of a dense row-major M x N matrix placed by L2 domain (the cudaMallocSided placement of
+    utility/sidedgpu.cu:791-838 applied to the GEMV's A): the first rows_side[0] rows live only in
+    granules homed in domain 0, the rest only in domain-1 granules.  ``pack(A)`` copies A in;
+    ``gemv(x, y, mode)`` computes y = A.x, in AWARE mode from near granules only."""
+
+    def __init__(self, M: int, N: int, dtype_in: int = F16, dtype_out: Optional[int] = None, device: int = 0,
+                 static_a: bool = False):
+        self._s = C.c_void_p(0)
+        self.M, self.N, self.device = M, N, device
+        desc = GemvDesc(M=M, N=N, lda=0, dtype_in=dtype_in, dtype_out=dtype_in if dtype_out is None else dtype_out,
+                        batch=1, stride_a=0, stride_x=0, stride_y=0, device=device, A=None,
+                        flags=PLAN_STATIC_A if static_a else 0)
+        check(lib().l2d_sided_create(C.byref(desc), C.byref(self._s)))
+
+    def pack(self, A, lda: int = 0, stream=None) -> None:
+        check(lib().l2d_sided_pack(self._s, _ptr(A), lda, _stream_handle(stream)))
+
+    def gemv(self, x, y, mode: int = MODE_AWARE, stream=None) -> None:
+        check(lib().l2d_gemv_sided(self._s, _ptr(x), _ptr(y), mode, _stream_handle(stream)))
+
+    def info(self) -> dict:
+        i = SidedInfo()
+        check(lib().l2d_sided_info(self._s, C.byref(i)))
+        return {"rows_side": list(i.rows_side), "granules_per_row": i.granules_per_row, "base": i.base or 0,
+                "bytes": i.bytes, "mask": i.mask}
+
+    def row_granules(self, row: int) -> list:
+        n = C.c_int(0)
+        check(lib().l2d_sided_row_granules(self._s, row, None, 0, C.byref(n)))
+        a = (C.c_uint64 * n.value)()
+        check(lib().l2d_sided_row_granules(self._s, row, a, n.value, C.byref(n)))
+        return list(a)
+
+    def close(self) -> None:
+        if self._s and self._s.value:
+            check(lib().l2d_sided_destroy(self._s))
+            self._s = C.c_void_p(0)
 
     def __del__(self):
         try:
