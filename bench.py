@@ -335,10 +335,6 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
     us = per_mode(plan, A, x, y, 1000)
     A2, xv, yv = A.view(tdt[dt]).view(M, N), x.view(tdt[dt]), y.view(tdt[dt])
     us["cublas_torch_mv"] = round(kernel_time_us(lambda: torch.mv(A2, xv, out=yv), 1000, stream), 3)
-    ps = L.GemvPlan(A, M, N, dt, dt, device=local, static_a=True)  # A written once: copies start early
-    for name, mode in (("aware", 1), ("stream", 3)):
-        us[f"{name}_static_a"] = round(kernel_time_us(lambda m=mode: ps.gemv(A, x, y, m, stream), 1000, stream), 3)
-    ps.close()
     g = gbs(nbytes, us)
     out["cfg2"] = {"workload": "fp16 4096x4096 (32 MiB), 1000 back-to-back calls, no flush (L2-resident)",
                    "bound": "l2", "us": us, "gbs": g, "l2_read_peak_gbs": l2_peak,
@@ -609,10 +605,6 @@ def run_ours(args, rank, world, local):
             out = torch.empty(m_loc, dtype=tdt, device=dev)
             A2 = A.view(tdt).view(m_loc, N)
             modes_us["cublas_torch_mv"] = round(kernel_time(lambda: torch.mv(A2, xv, out=out), args.steps), 3)
-        ps = L.GemvPlan(A, m_loc, N, dt, dt, batch=batch, device=local, static_a=True)
-        modes_us["aware_static_a"] = round(kernel_time(lambda: ps.gemv(A, x, y_loc, L.MODE_AWARE, stream),
-                                                       args.steps), 3)
-        ps.close()
         Ai = A.view(torch.int64)
         modes_us["torch_sum_read"] = round(kernel_time(lambda: torch.sum(Ai), max(5, args.steps // 5)), 3)
 

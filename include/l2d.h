@@ -201,12 +201,7 @@ enum {
                               shared-memory rings) for every mode when the shape allows them (rows on
                               4 KiB boundaries, x in shared memory); by default the plan picks them
                               per call where they were measured faster */
-    L2D_PLAN_NO_TMA = 4,   /* never use the granule-ring kernels */
-    L2D_PLAN_STATIC_A = 8  /* the caller guarantees that A is never written by the kernel launched on the
-                              stream immediately before a call (weights written once, then read by
-                              many calls): a ring call then starts copying A while the previous
-                              GEMV on the stream drains, instead of after it completes.  x and y are
-                              touched only after the previous kernel completed, either way. */
+    L2D_PLAN_NO_TMA = 4    /* never use the granule-ring kernels */
 };
 
 typedef struct {

@@ -33,7 +33,6 @@ MODES = {"oblivious": MODE_OBLIVIOUS, "baseline": MODE_OBLIVIOUS, "aware": MODE_
 PLAN_NO_PROBE = 1
 PLAN_TMA = 2      # granule-ring kernels for every mode (when the shape allows them)
 PLAN_NO_TMA = 4   # register kernels only; default: picked per call
-PLAN_STATIC_A = 8  # A is never written by the kernel right before a call: ring calls copy A early
 PAGE_BYTES = 2 * 1024 * 1024
 
 OK = 0
@@ -370,15 +369,13 @@ class GemvPlan:
 
     def __init__(self, A, M: int, N: int, dtype_in: int = F32, dtype_out: Optional[int] = None, lda: int = 0,
                  batch: int = 1, stride_a: int = 0, stride_x: int = 0, stride_y: int = 0, device: int = 0,
-                 domains: Optional[DomainModel] = None, probe: bool = True, tma: Optional[bool] = None,
-                 static_a: bool = False):
+                 domains: Optional[DomainModel] = None, probe: bool = True, tma: Optional[bool] = None):
         self._plan = C.c_void_p(0)
         self.desc = GemvDesc(M=M, N=N, lda=lda, dtype_in=dtype_in,
                              dtype_out=dtype_in if dtype_out is None else dtype_out, batch=batch,
                              stride_a=stride_a, stride_x=stride_x, stride_y=stride_y, device=device,
                              A=_ptr(A), flags=(0 if probe else PLAN_NO_PROBE) |
-                             (0 if tma is None else PLAN_TMA if tma else PLAN_NO_TMA) |
-                             (PLAN_STATIC_A if static_a else 0))
+                             (0 if tma is None else PLAN_TMA if tma else PLAN_NO_TMA))
         dm = None
         if domains is not None:
             self._sm = (C.c_int * len(domains.sm_domain))(*domains.sm_domain)
@@ -428,13 +425,11 @@ class SidedMatrix:
     granules homed in domain 0, the rest only in domain-1 granules.  ``pack(A)`` copies A in;
     ``gemv(x, y, mode)`` computes y = A.x, in AWARE mode from near granules only."""
 
-    def __init__(self, M: int, N: int, dtype_in: int = F16, dtype_out: Optional[int] = None, device: int = 0,
-                 static_a: bool = False):
+    def __init__(self, M: int, N: int, dtype_in: int = F16, dtype_out: Optional[int] = None, device: int = 0):
         self._s = C.c_void_p(0)
         self.M, self.N, self.device = M, N, device
         desc = GemvDesc(M=M, N=N, lda=0, dtype_in=dtype_in, dtype_out=dtype_in if dtype_out is None else dtype_out,
-                        batch=1, stride_a=0, stride_x=0, stride_y=0, device=device, A=None,
-                        flags=PLAN_STATIC_A if static_a else 0)
+                        batch=1, stride_a=0, stride_x=0, stride_y=0, device=device, A=None, flags=0)
         check(lib().l2d_sided_create(C.byref(desc), C.byref(self._s)))
 
     def pack(self, A, lda: int = 0, stream=None) -> None:

@@ -153,45 +153,6 @@ def test_ring_calls_repeat_bit_identical_across_modes(dev):
     assert O.rel_l2(ref.astype(np.float64), ys[0].cpu().numpy()) <= TOL[L.BF16]
 
 
-def test_static_a_plan_gives_the_same_bits(dev):
-    """L2D_PLAN_STATIC_A lets a ring call copy A before the previous GEMV on the stream completes
-    (its claims use the counters of its own launch parity): eight back-to-back calls, modes
-    interleaved, give the bits of a default plan's calls, and a call right after x is rewritten by a
-    copy reads the new x."""
-    M, N = 3000, 8192
-    A_h, x_h = inputs(M, N, L.F16)
-    raw = torch.empty(A_h.nbytes + PAGE, dtype=torch.uint8, device="cuda")
-    off = (-raw.data_ptr()) % PAGE
-    A = raw[off: off + A_h.nbytes]
-    A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
-    x = to_dev(x_h)
-    x2 = x.flip(0).contiguous()
-    ref_plan = L.GemvPlan(A, M, N, L.F16, L.F32)
-    plan = L.GemvPlan(A, M, N, L.F16, L.F32, static_a=True)
-    modes = [L.MODE_AWARE, L.MODE_STREAM, L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_OBLIVIOUS, L.MODE_AWARE,
-             L.MODE_STREAM, L.MODE_AWARE]
-    want = {}
-    for m in set(modes):
-        for xx, tag in ((x, 0), (x2, 1)):
-            y = torch.empty(M, dtype=torch.float32, device="cuda")
-            ref_plan.gemv(A, xx, y, m)
-            want[(m, tag)] = y
-    torch.cuda.synchronize()
-    xb = x.clone()
-    outs = [torch.empty(M, dtype=torch.float32, device="cuda") for _ in modes]
-    for i, (m, y) in enumerate(zip(modes, outs)):
-        if i == 5:
-            xb.copy_(x2)  # a copy between two calls: the next call must see it
-        plan.gemv(A, xb, y, m)
-    torch.cuda.synchronize()
-    for i, (m, y) in enumerate(zip(modes, outs)):
-        assert torch.equal(y, want[(m, 1 if i >= 5 else 0)]), f"call {i} mode {m}"
-    st = plan.stats()
-    assert st["calls"] == len(modes) and st["device_errors"] == 0
-    plan.close()
-    ref_plan.close()
-
-
 def test_ring_kernels_agree_with_register_kernels(dev):
     M, N = 4096, 8192
     A, x = inputs(M, N, L.BF16)
