@@ -1,10 +1,11 @@
 """One GEMV configuration, a few calls, for profiling with ncu (or timing a single shape).
 
     python -m l2domain_b200.gemv.profile_call --mib 32 --n 4096 --dtype fp16 --mode aware --warmup 5
-        [--layout dense|sided|sharded] [--calls 1]
+        [--layout dense|sided|sharded] [--kernel auto|ring|register] [--batch 1] [--calls 1]
 
 Builds a synthetic A of about `mib` MiB with rows of `n` elements (A ~ N(0, 0.02), x ~ N(0, 1),
-seed 0), plans it (which runs the SM and address probes once), then makes `warmup` calls and
+seed 0; `batch` problems of that size back to back), plans it (which runs the SM and address
+probes once), then makes `warmup` calls and
 `calls` more of one mode, so a capture can skip the warm-up launches (ncu -k regex:k_gemv -s W).
 Layouts: the dense plan (l2d_gemv), the same matrix packed by L2 domain (l2d_gemv_sided), or a
 one-rank peer-memory shard (l2d_gemv_sharded, the kernels the multi-GPU step runs).  Prints the mean
@@ -30,6 +31,8 @@ def main() -> int:
     ap.add_argument("--dtype", choices=sorted(L.DTYPES), default="fp16")
     ap.add_argument("--mode", choices=["aware", "oblivious", "swapped", "stream"], default="aware")
     ap.add_argument("--layout", choices=["dense", "sided", "sharded"], default="dense")
+    ap.add_argument("--kernel", choices=["auto", "ring", "register"], default="auto")
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--calls", type=int, default=1)
     args = ap.parse_args()
@@ -42,18 +45,22 @@ def main() -> int:
     eb = L.ELEM_BYTES[dt]
     N = args.n
     M = max(1, args.mib * 2**20 // (N * eb))
-    nb = M * N * eb
+    B = max(1, args.batch)
+    nb = B * M * N * eb
     raw = torch.empty(nb + (2 << 20), dtype=torch.uint8, device=dev)
     off = (-raw.data_ptr()) % (2 << 20)
     A = raw[off: off + nb]
-    L.fill_cfg(A, dt, M * N, 0, 0, 1, 0.0, 0.02)
-    x = torch.empty(N * eb, dtype=torch.uint8, device=dev)
-    L.fill_cfg(x, dt, N, 0, 1, 1, 0.0, 1.0)
-    y = torch.empty(M * eb, dtype=torch.uint8, device=dev)
+    L.fill_cfg(A, dt, B * M * N, 0, 0, 1, 0.0, 0.02)
+    x = torch.empty(B * N * eb, dtype=torch.uint8, device=dev)
+    L.fill_cfg(x, dt, B * N, 0, 1, 1, 0.0, 1.0)
+    y = torch.empty(B * M * eb, dtype=torch.uint8, device=dev)
+    tma = {"auto": None, "ring": True, "register": False}[args.kernel]
+    if B > 1 and args.layout != "dense":
+        raise SystemExit("--batch applies to the dense layout")
     mode = L.MODES[args.mode]
     closers = []
     if args.layout == "dense":
-        plan = L.GemvPlan(A, M, N, dt, dt)
+        plan = L.GemvPlan(A, M, N, dt, dt, batch=B, tma=tma)
         closers.append(plan)
         call = lambda: plan.gemv(A, x, y, mode)  # noqa: E731
     elif args.layout == "sided":
@@ -81,8 +88,8 @@ def main() -> int:
     us = a.elapsed_time(b) / args.calls * 1e3
     for c in closers:
         c.close()
-    print(json.dumps({"M": M, "N": N, "dtype": args.dtype, "mode": args.mode, "layout": args.layout,
-                      "bytes": nb, "us_per_call": round(us, 3)}))
+    print(json.dumps({"M": M, "N": N, "batch": B, "dtype": args.dtype, "mode": args.mode, "layout": args.layout,
+                      "kernel": args.kernel, "bytes": nb, "us_per_call": round(us, 3)}))
     return 0
 
 
