@@ -322,22 +322,24 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
         s.close()
         return res
 
-    def read_gbs(buf, nbytes, calls):
+    def read_gbs(buf, nbytes, calls, passes=1):
         nb = nbytes // 32 * 32
-        return round(nb / (kernel_time_us(lambda: L.read_stream(buf, nb, sink, 4096, local, stream), calls, stream)
-                           * 1e-6) / 1e9, 1)
+        us = kernel_time_us(lambda: L.read_stream(buf, nb, sink, 4096, local, stream, passes=passes), calls, stream)
+        return round(nb * passes / (us * 1e-6) / 1e9, 1)
 
     # Config 2: L2-resident fp16 4096x4096, 1000 back-to-back calls, against the L2 read peak.
     M, N, dt = 4096, 4096, F16
     raw, A, x, y, plan = setup(M, N, dt, (NORMAL, 0.0, 0.02), (NORMAL, 0.0, 1.0))
     nbytes = M * N * 2 + N * 2 + M * 2
-    l2_peak = read_gbs(A, M * N * 2, 1000)
+    l2_peak = read_gbs(A, M * N * 2, 20, passes=50)  # 50 passes over the L2-resident 32 MiB per launch
+    l2_launch = read_gbs(A, M * N * 2, 1000)          # one pass per launch: launch-bound like the GEMV
     us = per_mode(plan, A, x, y, 1000)
     A2, xv, yv = A.view(tdt[dt]).view(M, N), x.view(tdt[dt]), y.view(tdt[dt])
     us["cublas_torch_mv"] = round(kernel_time_us(lambda: torch.mv(A2, xv, out=yv), 1000, stream), 3)
     g = gbs(nbytes, us)
     out["cfg2"] = {"workload": "fp16 4096x4096 (32 MiB), 1000 back-to-back calls, no flush (L2-resident)",
                    "bound": "l2", "us": us, "gbs": g, "l2_read_peak_gbs": l2_peak,
+                   "read_stream_one_pass_per_launch_gbs": l2_launch,
                    "frac_of_l2_read_peak": {k: round(v / l2_peak, 4) for k, v in g.items()},
                    "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 200, 20, 0),
                    "sided_us": sided_us(A, x, y, M, N, dt, 1000)}
@@ -352,6 +354,7 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
     g = gbs(M * N * 2 + N * 2 + M * 2, us)
     out["l2_window"] = {"workload": "fp16 3584x16384 (112 MiB), 500 back-to-back calls, no flush", "bound": "l2",
                         "us": us, "gbs": g, "read_stream_gbs": read_gbs(A, M * N * 2, 500),
+                        "read_stream_gbs_20_passes_per_launch": read_gbs(A, M * N * 2, 20, passes=20),
                         "aware_speedup_vs_stream": round(us["stream"] / us["aware"], 4),
                         "aware_speedup_vs_oblivious": round(us["oblivious"] / us["aware"], 4),
                         "swapped_slowdown_vs_aware": round(us["swapped"] / us["aware"], 4),

@@ -353,11 +353,12 @@ L2D_API int l2d_fill_cfg(void *dst, int dtype, uint64_t first, uint64_t n, uint6
                          int dist, float p0, float p1, void *stream_handle);
 /* Evicts the L2 by writing a device buffer of the L2's size (GlobalL2Cache::reset). */
 L2D_API int l2d_l2_flush(int device, void *stream_handle);
-/* Read-only stream over [p, p + bytes): every byte is read once by 32-byte loads, one XOR word per
- * CTA lands in sink (one CTA per SM: sink_words >= the SM count).  p 32-byte aligned, bytes a
- * multiple of 32.  The bandwidth denominator of a read-dominated kernel: HBM read bandwidth over a
- * buffer larger than L2, L2 read bandwidth over an L2-resident buffer read back to back. */
-L2D_API int l2d_read_stream(int device, const void *p, size_t bytes, uint32_t *sink, size_t sink_words,
+/* Read-only stream over [p, p + bytes), `passes` times in one launch: every byte is read by 32-byte
+ * loads, one XOR word per CTA lands in sink (one CTA per SM: sink_words >= the SM count).  p 32-byte
+ * aligned, bytes a multiple of 32.  The bandwidth denominator of a read-dominated kernel: HBM read
+ * bandwidth over a buffer larger than L2 (passes = 1), L2 read bandwidth over an L2-resident
+ * buffer read many times in one launch. */
+L2D_API int l2d_read_stream(int device, const void *p, size_t bytes, int passes, uint32_t *sink, size_t sink_words,
                             void *stream_handle);
 /* Device properties the roofline needs. */
 L2D_API int l2d_device_info(int device, int *num_sm, int *l2_bytes, int *cc_major, int *cc_minor, char *name,

@@ -145,7 +145,7 @@ SIGNATURES = {
     "l2d_fill_ref": (_i, [_vp, _i, _u64, _u64, _u32, _i, _i, _vp]),
     "l2d_fill_cfg": (_i, [_vp, _i, _u64, _u64, _u64, _u64, _i, C.c_float, C.c_float, _vp]),
     "l2d_l2_flush": (_i, [_i, _vp]),
-    "l2d_read_stream": (_i, [_i, _vp, _sz, _vp, _sz, _vp]),
+    "l2d_read_stream": (_i, [_i, _vp, _sz, _i, _vp, _sz, _vp]),
     "l2d_device_info": (_i, [_i, _pi, _pi, _pi, _pi, C.c_char_p, _i]),
 }
 
@@ -614,9 +614,10 @@ def l2_flush(device: int = 0, stream=None) -> None:
     check(lib().l2d_l2_flush(device, _stream_handle(stream)))
 
 
-def read_stream(buf, nbytes: int, sink, sink_words: int, device: int = 0, stream=None) -> None:
-    """Reads [buf, buf + nbytes) once (the read-bandwidth roofline helper); sink holds one word per SM."""
-    check(lib().l2d_read_stream(device, _ptr(buf), nbytes, _ptr(sink), sink_words, _stream_handle(stream)))
+def read_stream(buf, nbytes: int, sink, sink_words: int, device: int = 0, stream=None, passes: int = 1) -> None:
+    """Reads [buf, buf + nbytes) `passes` times in one launch (the read-bandwidth roofline helper);
+    sink holds one word per SM."""
+    check(lib().l2d_read_stream(device, _ptr(buf), nbytes, passes, _ptr(sink), sink_words, _stream_handle(stream)))
 
 
 def device_info(device: int = 0) -> dict:

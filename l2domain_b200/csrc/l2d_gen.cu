@@ -168,33 +168,34 @@ int fill_grid(uint64_t n) {
 std::mutex g_flush_mu;
 std::map<int, std::pair<void *, size_t>> g_flush;  // device -> flush buffer (kept until exit)
 
-// Read-only stream: every 32-byte chunk of [p, p + n32 * 32) is loaded once (256-bit non-coherent
-// loads that do not allocate in L1, 4 in flight per thread, 128 KiB per SM) and folded into one
-// XOR word per CTA, so the loads cannot be elided.  The roofline denominators for a read-dominated
-// kernel: over a buffer larger than L2 it gives the HBM read bandwidth, over an L2-resident buffer
-// read back to back the L2 read bandwidth.
-__global__ void __launch_bounds__(1024) k_read_stream(const uint8_t *p, uint64_t n32, uint32_t *sink) {
+// Read-only stream: every 32-byte chunk of [p, p + n32 * 32) is loaded once per pass (256-bit
+// non-coherent loads that do not allocate in L1, 4 in flight per thread, 128 KiB per SM) and folded
+// into one XOR word per CTA, so the loads cannot be elided.  The roofline denominators for a
+// read-dominated kernel: over a buffer larger than L2 it gives the HBM read bandwidth; over an
+// L2-resident buffer read `passes` times in one launch, the L2 read bandwidth without the launch in
+// it (no load allocates in L1, so a repeated pass is served by L2, not by the SM's own cache).
+__device__ __forceinline__ uint32_t ld_xor32(const uint8_t *q) {
+    uint32_t v[8];
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "l"(q));
+    return v[0] ^ v[1] ^ v[2] ^ v[3] ^ v[4] ^ v[5] ^ v[6] ^ v[7];
+}
+
+__global__ void __launch_bounds__(1024) k_read_stream(const uint8_t *p, uint64_t n32, uint32_t *sink, int passes) {
     constexpr int kU = 4;
     uint32_t acc = 0;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-    uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    for (; i + (kU - 1) * stride < n32; i += kU * stride) {
-        uint32_t v[kU][8];
+    for (int pass = 0; pass < passes; ++pass) {
+        uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+        for (; i + (kU - 1) * stride < n32; i += kU * stride) {
+            uint32_t v[kU];
 #pragma unroll
-        for (int u = 0; u < kU; ++u)
-            asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                         : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3]), "=r"(v[u][4]), "=r"(v[u][5]),
-                           "=r"(v[u][6]), "=r"(v[u][7])
-                         : "l"(p + (i + u * stride) * 32));
+            for (int u = 0; u < kU; ++u) v[u] = ld_xor32(p + (i + u * stride) * 32);
 #pragma unroll
-        for (int u = 0; u < kU; ++u)
-#pragma unroll
-            for (int k = 0; k < 8; ++k) acc ^= v[u][k];
-    }
-    for (; i < n32; i += stride) {
-        const uint4 *q = reinterpret_cast<const uint4 *>(p + i * 32);
-        const uint4 a = __ldg(q), b = __ldg(q + 1);
-        acc ^= a.x ^ a.y ^ a.z ^ a.w ^ b.x ^ b.y ^ b.z ^ b.w;
+            for (int u = 0; u < kU; ++u) acc ^= v[u];
+        }
+        for (; i < n32; i += stride) acc ^= ld_xor32(p + i * 32);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc ^= __shfl_xor_sync(0xffffffffu, acc, o);
@@ -264,8 +265,10 @@ int l2d_l2_flush(int device, void *stream_handle) {
     return L2D_OK;
 }
 
-int l2d_read_stream(int device, const void *p, size_t bytes, uint32_t *sink, size_t sink_words, void *stream_handle) {
+int l2d_read_stream(int device, const void *p, size_t bytes, int passes, uint32_t *sink, size_t sink_words,
+                    void *stream_handle) {
     clear_error();
+    if (passes < 1) return set_error(L2D_ERR_INVALID, "read_stream: passes must be >= 1");
     if (!p || !sink || (reinterpret_cast<uintptr_t>(p) & 31) || (bytes & 31))
         return set_error(L2D_ERR_INVALID, "read_stream: p must be 32-byte aligned and bytes a multiple of 32");
     int num_sm = 0;
@@ -277,7 +280,7 @@ int l2d_read_stream(int device, const void *p, size_t bytes, uint32_t *sink, siz
     cudaGetDevice(&prev);
     if (prev != device) L2D_CUDA_TRY(cudaSetDevice(device));
     gen::k_read_stream<<<num_sm, 1024, 0, static_cast<cudaStream_t>(stream_handle)>>>(
-        static_cast<const uint8_t *>(p), bytes / 32, sink);
+        static_cast<const uint8_t *>(p), bytes / 32, sink, passes);
     cudaError_t e = cudaGetLastError();
     if (prev >= 0 && prev != device) cudaSetDevice(prev);
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "read_stream: %s", cudaGetErrorString(e));
