@@ -225,6 +225,7 @@ def run_reference(args, rank, world):
 # ------------------------------------------------------------------------------------------------
 
 MODE_NAMES = (("aware", 1), ("oblivious", 0), ("swapped", 2), ("stream", 3))
+PLACEMENTS = ("granules", "rows")  # l2d_plan_stats.placement 0 / 1
 
 
 def kernel_time_us(fn, steps, stream, barrier=None, reduce=None, warm=3):
@@ -322,6 +323,16 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
         s.close()
         return res
 
+    def other_placement(plan, A, x, y, M, N, dt, calls, batch=1):
+        """The split modes under the placement the plan did not pick (granules <-> whole rows)."""
+        mine = plan.stats()["placement"]
+        other = "granules" if mine == 1 else "rows"
+        p2 = L.GemvPlan(A, M, N, dt, dt, batch=batch, device=local, placement=other)
+        res = {name: round(kernel_time_us(lambda m=mode: p2.gemv(A, x, y, m, stream), calls, stream), 3)
+               for name, mode in MODE_NAMES if mode != 3}
+        p2.close()
+        return {"plan_placement": PLACEMENTS[mine], "other_placement": other, "us": res}
+
     def read_gbs(buf, nbytes, calls, passes=1):
         nb = nbytes // 32 * 32
         us = kernel_time_us(lambda: L.read_stream(buf, nb, sink, 4096, local, stream, passes=passes), calls, stream)
@@ -342,7 +353,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                    "read_stream_one_pass_per_launch_gbs": l2_launch,
                    "frac_of_l2_read_peak": {k: round(v / l2_peak, 4) for k, v in g.items()},
                    "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 200, 20, 0),
-                   "sided_us": sided_us(A, x, y, M, N, dt, 1000)}
+                   "sided_us": sided_us(A, x, y, M, N, dt, 1000),
+                   "placements": other_placement(plan, A, x, y, M, N, dt, 1000)}
     plan.close()
     del raw, A
 
@@ -358,7 +370,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                         "aware_speedup_vs_stream": round(us["stream"] / us["aware"], 4),
                         "aware_speedup_vs_oblivious": round(us["oblivious"] / us["aware"], 4),
                         "swapped_slowdown_vs_aware": round(us["swapped"] / us["aware"], 4),
-                        "sided_us": sided_us(A, x, y, M, N, dt, 500)}
+                        "sided_us": sided_us(A, x, y, M, N, dt, 500),
+                        "placements": other_placement(plan, A, x, y, M, N, dt, 500)}
     plan.close()
     del raw, A
 
@@ -382,7 +395,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                                           "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in gf.items()}
                                           if read_peak else None},
                    "back_to_back": {"protocol": "200 back-to-back calls, no flush (64 MiB stays in L2)", "bound": "l2",
-                                    "us": steady, "gbs": gbs(nbytes, steady)}}
+                                    "us": steady, "gbs": gbs(nbytes, steady),
+                                    "placements": other_placement(plan, A, x, y, M, N, dt, 200)}}
     plan.close()
     del raw, A
 
@@ -399,7 +413,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                    "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in g.items()} if read_peak else None,
                    "frac_of_copy_peak": {k: round(v / copy_peak, 4) for k, v in g.items()},
                    "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 20, 5, 0),
-                   "sided_us": sided_us(A, x, y, M, N, dt, 50)}
+                   "sided_us": sided_us(A, x, y, M, N, dt, 50),
+                   "placements": other_placement(plan, A, x, y, M, N, dt, 50)}
     plan.close()
     del raw, A
 
@@ -415,7 +430,8 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
     out["cfg4"] = {"workload": "fp16 32 x (8192x8192) contiguous batch (4 GiB), 10 back-to-back calls",
                    "bound": "hbm", "us": us, "gbs": g,
                    "frac_of_read_peak": {k: round(v / read_peak, 4) for k, v in g.items()} if read_peak else None,
-                   "kernel": "ring (TMA bulk copies)" if plan.stats()["ring_modes"] & 2 else "register"}
+                   "kernel": "ring (TMA bulk copies)" if plan.stats()["ring_modes"] & 2 else "register",
+                   "placements": other_placement(plan, A, x, y, M, N, dt, 10, batch=B)}
     plan.close()
     del raw, A
     torch.cuda.empty_cache()
@@ -694,7 +710,7 @@ def run_ours(args, rank, world, local):
             "plan": {"probe_and_plan_s": round(t_plan, 3), "domain_sms": pstats["domain_sms"],
                      "granule_shift": pstats["granule_shift"], "domain_bytes": pstats["domain_bytes"],
                      "split_rows": pstats["split_rows"], "fallback_slots": fstats["fallback_slots"],
-                     "calls": fstats["calls"],
+                     "calls": fstats["calls"], "placement": PLACEMENTS[pstats["placement"]],
                      "kernel": "ring (TMA bulk copies)" if fstats["ring_modes"] & (1 << L.MODE_AWARE) else "register"},
             "check": {"rows_per_rank": 64, "rel_l2_vs_torch_f64_worst_rank": rel,
                       "p2p_gather_equals_nccl": gather_exact},

@@ -201,7 +201,14 @@ enum {
                               shared-memory rings) for every mode when the shape allows them (rows on
                               4 KiB boundaries, x in shared memory); by default the plan picks them
                               per call where they were measured faster */
-    L2D_PLAN_NO_TMA = 4    /* never use the granule-ring kernels */
+    L2D_PLAN_NO_TMA = 4,   /* never use the granule-ring kernels */
+    /* Placement of the split modes (AWARE, SWAPPED, OBLIVIOUS); by default the plan picks it from
+     * A's size against the L2 (see l2d_plan_stats.placement). */
+    L2D_PLAN_GRANULES = 8, /* every 4 KiB granule goes to the group of its domain: an SM reads only
+                              its own domain's granules, rows that span both domains are summed in
+                              two parts */
+    L2D_PLAN_ROWS = 16     /* every row goes whole to the group of its first granule's domain (the
+                              reference's placement, gemv_k1024_persistent_subwarp.cu:264-269) */
 };
 
 typedef struct {
@@ -229,6 +236,8 @@ typedef struct {
     int64_t ring_whole_rows;     /* ring calls in AWARE / OBLIVIOUS: the last rows, taken whole by either group */
     int64_t ring_chunk_rows;     /* ring calls: rows per claim from a row pool */
     int sm_map_cached;           /* 1: the SM map was read from the domain-map cache, 0: probed or given */
+    int placement;               /* split modes: 0 granules, 1 whole rows (L2D_PLAN_GRANULES / _ROWS) */
+    int64_t row_domain_bytes[2]; /* A bytes in rows whose first granule is homed in each domain */
 } l2d_plan_stats;
 
 /* Creates a plan.  map == NULL probes the device and desc->A's region (2 MiB pages covering

@@ -33,6 +33,8 @@ MODES = {"oblivious": MODE_OBLIVIOUS, "baseline": MODE_OBLIVIOUS, "aware": MODE_
 PLAN_NO_PROBE = 1
 PLAN_TMA = 2      # granule-ring kernels for every mode (when the shape allows them)
 PLAN_NO_TMA = 4   # register kernels only; default: picked per call
+PLAN_GRANULES = 8  # split modes place 4 KiB granules by domain (rows that span both are summed in two parts)
+PLAN_ROWS = 16     # split modes place whole rows by their first granule's domain (the reference's rule)
 PAGE_BYTES = 2 * 1024 * 1024
 
 OK = 0
@@ -83,7 +85,8 @@ class PlanStats(C.Structure):
                 ("split_rows", C.c_int64), ("domain_sms", C.c_int * 2), ("grid", C.c_int), ("block", C.c_int),
                 ("scratch_bytes", C.c_size_t), ("fallback_slots", C.c_uint64), ("calls", C.c_uint64),
                 ("tma", C.c_int), ("device_errors", C.c_uint64), ("ring_modes", C.c_int),
-                ("ring_whole_rows", C.c_int64), ("ring_chunk_rows", C.c_int64), ("sm_map_cached", C.c_int)]
+                ("ring_whole_rows", C.c_int64), ("ring_chunk_rows", C.c_int64), ("sm_map_cached", C.c_int),
+                ("placement", C.c_int), ("row_domain_bytes", C.c_int64 * 2)]
 
 
 # Every symbol include/l2d.h declares, with its ctypes signature.
@@ -365,17 +368,21 @@ class GemvPlan:
     """A GEMV plan for one A allocation: y = A.x (batched optional), fp32 accumulation.
 
     ``tma``: None picks the granule-ring (TMA) or register kernels per call, True uses the rings
-    for every call the shape allows, False only the register kernels."""
+    for every call the shape allows, False only the register kernels.  ``placement`` ("granules",
+    "rows" or None for the plan's choice): how the split modes divide A between the two domain
+    groups -- granule by granule, or whole rows by the domain of their first granule."""
 
     def __init__(self, A, M: int, N: int, dtype_in: int = F32, dtype_out: Optional[int] = None, lda: int = 0,
                  batch: int = 1, stride_a: int = 0, stride_x: int = 0, stride_y: int = 0, device: int = 0,
-                 domains: Optional[DomainModel] = None, probe: bool = True, tma: Optional[bool] = None):
+                 domains: Optional[DomainModel] = None, probe: bool = True, tma: Optional[bool] = None,
+                 placement: Optional[str] = None):
         self._plan = C.c_void_p(0)
         self.desc = GemvDesc(M=M, N=N, lda=lda, dtype_in=dtype_in,
                              dtype_out=dtype_in if dtype_out is None else dtype_out, batch=batch,
                              stride_a=stride_a, stride_x=stride_x, stride_y=stride_y, device=device,
                              A=_ptr(A), flags=(0 if probe else PLAN_NO_PROBE) |
-                             (0 if tma is None else PLAN_TMA if tma else PLAN_NO_TMA))
+                             (0 if tma is None else PLAN_TMA if tma else PLAN_NO_TMA) |
+                             {None: 0, "granules": PLAN_GRANULES, "rows": PLAN_ROWS}[placement])
         dm = None
         if domains is not None:
             self._sm = (C.c_int * len(domains.sm_domain))(*domains.sm_domain)

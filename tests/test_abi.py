@@ -313,3 +313,14 @@ def test_plan_without_gpu_reports_no_device():
     with pytest.raises(L.L2DError) as e:
         L.GemvPlan(0x10000000, 16, 16)
     assert e.value.status == -3
+
+
+def test_plan_placement_flags_exclude_each_other():
+    """L2D_PLAN_GRANULES with L2D_PLAN_ROWS is refused before any device is touched."""
+    desc = L.GemvDesc(M=16, N=16, lda=0, dtype_in=L.F32, dtype_out=L.F32, batch=1, stride_a=0, stride_x=0,
+                      stride_y=0, device=0, A=0x10000000, flags=L.PLAN_GRANULES | L.PLAN_ROWS)
+    plan = C.c_void_p(0)
+    assert L.lib().l2d_plan_create(C.byref(desc), None, C.byref(plan)) == -1
+    assert b"exclude" in L.lib().l2d_last_error()
+    with pytest.raises(KeyError):
+        L.GemvPlan(0x10000000, 16, 16, placement="pages")

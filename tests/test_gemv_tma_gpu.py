@@ -52,14 +52,14 @@ def inputs(M, N, dtype, batch=1, kind="cfg"):
     return O.round_to(A32, dtype), O.round_to(x32, dtype)
 
 
-def run(A_h, x_h, M, N, dtype, dtype_out, modes, batch=1, tma=True):
+def run(A_h, x_h, M, N, dtype, dtype_out, modes, batch=1, tma=True, placement=None):
     nbytes = A_h.nbytes
     raw = torch.empty(nbytes + PAGE, dtype=torch.uint8, device="cuda")
     off = (-raw.data_ptr()) % PAGE
     A = raw[off: off + nbytes]
     A.copy_(to_dev(A_h).view(torch.uint8).reshape(-1))
     x = to_dev(x_h)
-    plan = L.GemvPlan(A, M, N, dtype, dtype_out, batch=batch, tma=tma)
+    plan = L.GemvPlan(A, M, N, dtype, dtype_out, batch=batch, tma=tma, placement=placement)
     outs = {}
     for mode in modes:
         if dtype_out == L.F32:
@@ -113,14 +113,15 @@ def test_ring_kernels_integer_kat_bit_exact(dev):
 def test_ring_kernels_aware_swapped_identical_and_deterministic(dev):
     M, N = 1024, 8192
     A, x = inputs(M, N, L.F16)
-    outs, stats = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_STREAM])
+    outs, stats = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE, L.MODE_SWAPPED, L.MODE_STREAM], placement="granules")
+    assert stats["placement"] == 0
     whole = stats["ring_whole_rows"]
     assert 0 < whole < M // 4 and stats["ring_chunk_rows"] >= 1
     pool = M - whole
     assert np.array_equal(outs[L.MODE_AWARE][:pool], outs[L.MODE_SWAPPED][:pool])
     # Whole rows (one warp, every granule in order) are STREAM's arithmetic exactly.
     assert np.array_equal(outs[L.MODE_AWARE][pool:], outs[L.MODE_STREAM][pool:])
-    outs2, _ = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE])
+    outs2, _ = run(A, x, M, N, L.F16, L.F32, [L.MODE_AWARE], placement="granules")
     assert np.array_equal(outs[L.MODE_AWARE], outs2[L.MODE_AWARE])
 
 
