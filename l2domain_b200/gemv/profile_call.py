@@ -1,7 +1,8 @@
 """One GEMV configuration, a few calls, for profiling with ncu (or timing a single shape).
 
     python -m l2domain_b200.gemv.profile_call --mib 32 --n 4096 --dtype fp16 --mode aware --warmup 5
-        [--layout dense|sided|sharded] [--kernel auto|ring|register] [--batch 1] [--calls 1]
+        [--layout dense|sided|sharded] [--kernel auto|ring|register] [--placement auto|granules|rows]
+        [--batch 1] [--calls 1]
 
 Builds a synthetic A of about `mib` MiB with rows of `n` elements (A ~ N(0, 0.02), x ~ N(0, 1),
 seed 0; `batch` problems of that size back to back), plans it (which runs the SM and address
@@ -32,6 +33,7 @@ def main() -> int:
     ap.add_argument("--mode", choices=["aware", "oblivious", "swapped", "stream"], default="aware")
     ap.add_argument("--layout", choices=["dense", "sided", "sharded"], default="dense")
     ap.add_argument("--kernel", choices=["auto", "ring", "register"], default="auto")
+    ap.add_argument("--placement", choices=["auto", "granules", "rows"], default="auto")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--calls", type=int, default=1)
@@ -60,7 +62,8 @@ def main() -> int:
     mode = L.MODES[args.mode]
     closers = []
     if args.layout == "dense":
-        plan = L.GemvPlan(A, M, N, dt, dt, batch=B, tma=tma)
+        plan = L.GemvPlan(A, M, N, dt, dt, batch=B, tma=tma,
+                          placement=None if args.placement == "auto" else args.placement)
         closers.append(plan)
         call = lambda: plan.gemv(A, x, y, mode)  # noqa: E731
     elif args.layout == "sided":
@@ -69,7 +72,7 @@ def main() -> int:
         closers.append(s)
         call = lambda: s.gemv(x, y, mode)  # noqa: E731
     else:
-        plan = L.GemvPlan(A, M, N, dt, dt)
+        plan = L.GemvPlan(A, M, N, dt, dt, placement=None if args.placement == "auto" else args.placement)
         sh = L.PeerShard(0, 0, 1, M, 0, M, N, dt, dt)
         sh.connect([sh.handle()])
         for par in (0, 1):
@@ -89,7 +92,7 @@ def main() -> int:
     for c in closers:
         c.close()
     print(json.dumps({"M": M, "N": N, "batch": B, "dtype": args.dtype, "mode": args.mode, "layout": args.layout,
-                      "kernel": args.kernel, "bytes": nb, "us_per_call": round(us, 3)}))
+                      "kernel": args.kernel, "placement": args.placement, "bytes": nb, "us_per_call": round(us, 3)}))
     return 0
 
 
