@@ -1149,11 +1149,20 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
                                          smem, true, &s_won, flag_old < a.call_no);
     __syncthreads();
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    if (tid == 0) s_done = atomicAdd(a.ctl + kCtlDone, 1ull | (static_cast<unsigned long long>(grp) << 32));
+    // Done count: bits 0-15 CTAs done, 16-31 slot flags won, 32-63 CTAs of group 1.
+    const bool won_slot = gslot >= 0 && s_won;  // s_won: thread 0's answer of the slot flag (walk_pools)
+    if (tid == 0)
+        s_done = atomicAdd(a.ctl + kCtlDone, 1ull | (won_slot ? 1ull << 16 : 0ull) |
+                                                 (static_cast<unsigned long long>(grp) << 32));
     __syncthreads();
     const unsigned long long before = s_done;
-    const bool last = static_cast<uint32_t>(before) + 1u == gridDim.x;
-    if (last) {
+    const bool last = static_cast<uint32_t>(before & 0xffffu) + 1u == gridDim.x;
+    // Every slot with first chunks won by a CTA of this launch (the common case): nothing to sweep,
+    // and the last CTA skips a round of flag loads before the grid can complete.
+    const uint32_t won_all = static_cast<uint32_t>((before >> 16) & 0xffffu) + (won_slot ? 1u : 0u);
+    const uint32_t with_first = SPLIT ? (a.first_chunks[0] > 0 ? a.n_dom0 : 0) + (a.first_chunks[1] > 0 ? a.n_slots - a.n_dom0 : 0)
+                                      : (a.first_chunks[0] > 0 ? a.n_slots : 0);
+    if (last && won_all != with_first) {
         // First chunks of slots that no CTA of this launch took (their SMs ran none of its CTAs).
         if (tid == 0) s_nleft = 0;
         if (tid < kMaxSmid / 32) s_left[tid] = 0u;
