@@ -742,8 +742,9 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 constexpr int kCtlEpoch = 0, kCtlDone = 1, kCtlFallback = 2, kCtlError = 3;
 // ctl[kCtlPool + 16 (3 p + c)]: pool counter c (0, 1, 2) of launches of parity p.  A ring launch
 // claims rows before the previous launch on the stream has completed (programmatic dependent
-// launch), so consecutive launches use different counters; the launch two back, which used these,
-// has completed before this one can start, and its last CTA left them at zero.
+// launch), so consecutive launches use different counters; the previous launch zeroed these once
+// the launch two back, which used them, had completed (ring_call).  ctl[kCtlDone]: the register
+// kernels' count of finished CTAs.
 constexpr int kCtlPool = 16;
 constexpr int kCtlWords = kCtlPool + 16 * 6;
 
@@ -946,13 +947,33 @@ template <bool SH> __device__ __forceinline__ void stage_x_start(const GemvArgs 
     if ((!SH || a.shard_rank == 0) && !a.x_glob) stage_x_issue(a, smem);
 }
 
+// Ring kernels: warp-wide search for a slot whose first-chunk flag this launch has not set yet;
+// sets it (atomicMax of the call number) and returns the slot, or -1 when every slot is taken.
+__device__ __forceinline__ int warp_claim_slot(const GemvArgs &a, int lane) {
+    unsigned long long *flags = a.rflag + static_cast<size_t>(a.pool_parity) * a.n_slots;
+    const unsigned long long E = a.call_no;
+    for (int base = 0; base < a.n_slots; base += 32) {
+        const int t = base + lane;
+        const bool cand = t < a.n_slots && ld_claim(flags + t) < E;
+        uint32_t m = __ballot_sync(0xffffffffu, cand);
+        while (m) {
+            const int l = __ffs(m) - 1;
+            m &= m - 1;
+            int ok = 0;
+            if (lane == l) ok = atomicMax(flags + t, E) < E;
+            if (__shfl_sync(0xffffffffu, ok, l)) return base + l;
+        }
+    }
+    return -1;
+}
+
 // One warp's walk over the pools of group grp.  k_first / k_second: the warp's chunks of the CTA's
 // first claim (-1: claim from the start).  Before the first granule is consumed, x is staged
 // (stage_x_issue started its copies; SH: the flagged words), so the first copies of A overlap it.
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
 __device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long k_first, long long k_second,
                                            uint32_t tag, int warp, int lane, uint8_t *smem, bool stage_x_now,
-                                           int *s_won, bool won) {
+                                           int *s_won, bool won, int *s_adopt) {
     constexpr int eo = DT_OUT == L2D_F32 ? 4 : 2;
     uint8_t *ring = smem + a.ring_off;
     uint8_t *stages = ring + static_cast<size_t>(warp) * kTmaStages * kGranBytes;
@@ -970,7 +991,17 @@ __device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long
     __syncwarp();
     bool timed_out = false;
     if (stage_x_now) {
-        if (threadIdx.x == 0) *s_won = won;  // the slot flag's answer, long back by now
+        // The slot flag's answer, long back by now.  A CTA without a slot (a second CTA of this
+        // launch on its SM) takes over a slot no CTA has taken yet: one must exist (as many CTAs
+        // as slots, each holding at most one), and it is walked after this CTA's own walk.
+        if (warp == 0) {
+            const bool w0 = __shfl_sync(0xffffffffu, won, 0);
+            const int t = w0 ? -1 : warp_claim_slot(a, lane);
+            if (lane == 0) {
+                *s_won = w0;
+                *s_adopt = t;
+            }
+        }
         if (SH && a.shard_rank != 0) {
             shard_wait_x(a, smem);  // rank 0 pushed x and staged its own like an unsharded call
         } else {
@@ -1107,21 +1138,21 @@ __device__ __forceinline__ int group_rank(const GemvArgs &a, uint32_t sm, int gr
 //    takes chunks [i F, i F + F) of the group's first pool, F = first_chunks[g], one or two per
 //    warp, without touching a shared counter; the counters hand out the chunks after the first
 //    n_g F.  A flag per slot and launch parity (atomicMax of the call number, answered while x
-//    is staged) catches a second CTA of the launch on the same SM, which drops its copies and
-//    claims from the counters instead; the last CTA walks the first chunks of slots whose SM ran
-//    no CTA at all.
+//    is staged) catches a second CTA of the launch on the same SM: it drops its copies, claims
+//    from the counters instead, and takes over a slot that no CTA has set (walk_pools), whose
+//    first chunks and group pools it walks at its end.  Every slot is then walked by one CTA and
+//    every group with a slot by at least one, so no CTA needs to know that it finished last.
 //  * Until griddepcontrol.wait the launch may overlap the previous kernel on the stream, so it
 //    touches only its own state: the slot flag of its launch parity, the plan's attr words
 //    (written at plan creation), shared memory.  A, x and y come after the wait.
-//  * The done count carries each CTA's group in its high half, so the last CTA knows whether a
-//    group had no CTA at all and then walks that group's pools itself; it resets the counters of
-//    its launch parity for the launch after next.  No CTA reads another's results, so nothing
-//    here needs a fence.
+//  * The pool counters of the other launch parity belong to the previous ring launch, complete
+//    once the wait returns: CTA 0 zeroes them there for the launch after this one, whose own wait
+//    orders them before its claims.  CTA 0 also records the call number (the calls-done stat and
+//    the register kernels' epoch) at its end.  No CTA reads another's results, so nothing here
+//    needs a fence, and the grid ends with its last walk.
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH>
 __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
-    __shared__ unsigned long long s_done;
-    __shared__ int s_won, s_nleft;
-    __shared__ uint32_t s_left[kMaxSmid / 32];  // slots the last CTA took over (bit set)
+    __shared__ int s_won, s_adopt;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     const uint32_t sm = dev::smid();
     const int grp =
@@ -1130,9 +1161,9 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
     unsigned long long *flags = a.rflag + static_cast<size_t>(a.pool_parity) * a.n_slots;
     const int first = a.first_chunks[grp];
     int slot = -1;
-    if (first > 0 && sm < static_cast<uint32_t>(a.n_slots)) slot = SPLIT ? group_rank(a, sm, grp) : static_cast<int>(sm);
+    if (sm < static_cast<uint32_t>(a.n_slots)) slot = SPLIT ? group_rank(a, sm, grp) : static_cast<int>(sm);
     const int gslot = slot < 0 ? -1 : (SPLIT && grp ? a.n_dom0 + slot : slot);
-    unsigned long long flag_old = 0;
+    unsigned long long flag_old = ~0ull;
     if (tid == 0 && gslot >= 0) flag_old = atomicMax(flags + gslot, a.call_no);
     if ((SPLIT || a.sided) && a.dom_kind == 0 && a.attr_words <= kAttrSmemWords)
         for (int w = tid; w < a.attr_words; w += blockDim.x) s_attr[w] = __ldg(a.attr_bits + w);
@@ -1141,71 +1172,30 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
     if (tid < kTmaWarps) s_tma_count[tid] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // A, x and y may belong to the previous kernel
+    if (blockIdx.x == 0 && tid == 0)
+        for (int c = 0; c < 3; ++c) a.ctl[kCtlPool + 16 * (3 * (a.pool_parity ^ 1) + c)] = 0ull;
     stage_x_start<SH>(a, smem);
     __syncthreads();
-    const long long k0 = slot >= 0 ? static_cast<long long>(slot) * first : -1;
+    const long long k0 = slot >= 0 && first > 0 ? static_cast<long long>(slot) * first : -1;
     walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, grp, k0 >= 0 && warp < first ? k0 + warp : -1,
                                          k0 >= 0 && nwarps + warp < first ? k0 + nwarps + warp : -1, tag, warp, lane,
-                                         smem, true, &s_won, flag_old < a.call_no);
+                                         smem, true, &s_won, flag_old < a.call_no, &s_adopt);
     __syncthreads();
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // Done count: bits 0-15 CTAs done, 16-31 slot flags won, 32-63 CTAs of group 1.
-    const bool won_slot = gslot >= 0 && s_won;  // s_won: thread 0's answer of the slot flag (walk_pools)
-    if (tid == 0)
-        s_done = atomicAdd(a.ctl + kCtlDone, 1ull | (won_slot ? 1ull << 16 : 0ull) |
-                                                 (static_cast<unsigned long long>(grp) << 32));
-    __syncthreads();
-    const unsigned long long before = s_done;
-    const bool last = static_cast<uint32_t>(before & 0xffffu) + 1u == gridDim.x;
-    // Every slot with first chunks won by a CTA of this launch (the common case): nothing to sweep,
-    // and the last CTA skips a round of flag loads before the grid can complete.
-    const uint32_t won_all = static_cast<uint32_t>((before >> 16) & 0xffffu) + (won_slot ? 1u : 0u);
-    const uint32_t with_first = SPLIT ? (a.first_chunks[0] > 0 ? a.n_dom0 : 0) + (a.first_chunks[1] > 0 ? a.n_slots - a.n_dom0 : 0)
-                                      : (a.first_chunks[0] > 0 ? a.n_slots : 0);
-    if (last && won_all != with_first) {
-        // First chunks of slots that no CTA of this launch took (their SMs ran none of its CTAs).
-        if (tid == 0) s_nleft = 0;
-        if (tid < kMaxSmid / 32) s_left[tid] = 0u;
+    const int adopt = s_adopt;
+    if (adopt >= 0) {
+        // The slot this CTA took over: its first chunks, then (the walk goes on claiming) its
+        // group's pools, empty unless that group has no CTA of its own in this launch.
+        const int g = SPLIT && adopt >= a.n_dom0 ? 1 : 0;
+        const int F = a.first_chunks[g];
+        const long long kb = static_cast<long long>(adopt - (g ? a.n_dom0 : 0)) * F;
+        if (tid == 0) atomicAdd(a.ctl + kCtlFallback, 1ull);
+        walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, g, warp < F ? kb + warp : -1, nwarps + warp < F ? kb + nwarps + warp : -1,
+                                             tag, warp, lane, smem, false, nullptr, true, nullptr);
         __syncthreads();
-        for (int t = tid; t < a.n_slots; t += blockDim.x) {
-            const int g = SPLIT && t >= a.n_dom0 ? 1 : 0;
-            if (a.first_chunks[g] > 0 && ld_claim(flags + t) < a.call_no && atomicMax(flags + t, a.call_no) < a.call_no) {
-                atomicOr(&s_left[t >> 5], 1u << (t & 31));
-                atomicAdd(&s_nleft, 1);
-            }
-        }
-        __syncthreads();
-        const int n_left = s_nleft;
-        if (tid == 0 && n_left) atomicAdd(a.ctl + kCtlFallback, static_cast<unsigned long long>(n_left));
-        for (int wd = 0; n_left && wd < kMaxSmid / 32; ++wd) {
-            for (uint32_t m = s_left[wd]; m; m &= m - 1u) {
-                const int t = wd * 32 + __ffs(m) - 1;
-                const int g = SPLIT && t >= a.n_dom0 ? 1 : 0;
-                const int F = a.first_chunks[g];
-                const long long kb = static_cast<long long>(t - (g ? a.n_dom0 : 0)) * F;
-                walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, g, warp < F ? kb + warp : -1,
-                                                     nwarps + warp < F ? kb + nwarps + warp : -1, tag, warp, lane,
-                                                     smem, false, nullptr, true);
-                __syncthreads();
-            }
-        }
-    }
-    if (SPLIT && last) {
-        const uint32_t g1 = static_cast<uint32_t>(before >> 32) + static_cast<uint32_t>(grp);
-        const uint32_t g0 = gridDim.x - g1;
-        for (int g = 0; g < 2; ++g) {
-            if ((g ? g1 : g0) != 0u) continue;
-            if (tid == 0) atomicAdd(a.ctl + kCtlFallback, 1ull);
-            walk_pools<DT_IN, DT_OUT, SPLIT, SH>(a, g, -1, -1, tag, warp, lane, smem, false, nullptr, true);
-            __syncthreads();
-        }
     }
     shard_gather<DT_OUT, SH>(a);
-    if (last && tid == 0) {
-        for (int c = 0; c < 3; ++c) a.ctl[kCtlPool + 16 * (3 * a.pool_parity + c)] = 0ull;
-        a.ctl[kCtlDone] = 0ull;
-        *reinterpret_cast<volatile unsigned long long *>(a.ctl + kCtlEpoch) = a.call_no;
-    }
+    if (blockIdx.x == 0 && tid == 0) *reinterpret_cast<volatile unsigned long long *>(a.ctl + kCtlEpoch) = a.call_no;
 }
 
 template <int DT_IN, int DT_OUT, bool SPLIT, bool SH, bool TMA>
@@ -1227,7 +1217,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     __shared__ unsigned long long s_epoch;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     if (warp == 0) {
-        const unsigned long long E = ld_claim(a.ctl) + 1ull;
+        const unsigned long long E = ld_claim(a.ctl + kCtlEpoch) + 1ull;
         int got = -1;
         if (lane == 0) {
             const uint32_t sm = dev::smid();
@@ -1237,7 +1227,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
         got = __shfl_sync(0xffffffffu, got, 0);
         if (got < 0) {  // this SM's slot is taken (two CTAs on one SM): any unclaimed slot will do
             got = warp_claim_any(a, E, lane);
-            if (got >= 0 && lane == 0) atomicAdd(a.ctl + 2, 1ull);
+            if (got >= 0 && lane == 0) atomicAdd(a.ctl + kCtlFallback, 1ull);
         }
         if (lane == 0) {
             s_slot = got;
@@ -1253,7 +1243,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     if (tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid == 0) {
         __threadfence();
-        const unsigned long long done = atomicAdd(a.ctl + 1, 1ull);
+        const unsigned long long done = atomicAdd(a.ctl + kCtlDone, 1ull);
         s_last = done == gridDim.x - 1;
         if (s_last) __threadfence();  // acquire side: the other CTAs' y rows before the epilogue
     }
@@ -1272,7 +1262,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     }
     __syncthreads();
     const int n_left = s_count;
-    if (tid == 0 && n_left) atomicAdd(a.ctl + 2, static_cast<unsigned long long>(n_left));
+    if (tid == 0 && n_left) atomicAdd(a.ctl + kCtlFallback, static_cast<unsigned long long>(n_left));
     for (int w = 0; n_left && w < kMaxSmid / 32; ++w) {
         for (uint32_t m = s_left[w]; m; m &= m - 1u) {
             const int t = w * 32 + __ffs(m) - 1;
@@ -1282,9 +1272,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(GemvArgs a) {
     }
     shard_gather<DT_OUT, SH>(a);
     if (tid == 0) {
-        a.ctl[1] = 0ull;
+        a.ctl[kCtlDone] = 0ull;
         __threadfence();
-        *reinterpret_cast<volatile unsigned long long *>(a.ctl) = E;
+        *reinterpret_cast<volatile unsigned long long *>(a.ctl + kCtlEpoch) = E;
     }
 }
 

@@ -1,0 +1,123 @@
+"""GPU: a GEMV launch some of whose CTAs share an SM (other work holds SMs) still covers every row.
+
+Each GEMV kernel launches one CTA per SM slot and expects each CTA on its own SM; the CTA that
+finds its SM's slot already taken in this launch takes over a slot that no CTA has taken (the
+ring kernels walk that slot's first chunks and its group's pools at their end; the register kernels
+claim any free slot).  To get there, a helper kernel (compiled here with NVRTC) holds a few SMs with
+the whole of their shared memory for a bounded time (it reads %globaltimer and returns after
+`ns`), so the GEMV's CTAs for those SMs run later on SMs that already ran one.  The results must be
+the same bits as without the helper, and the plan counts the slots taken over.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import l2domain_b200 as L  # noqa: E402
+import oracle as O  # noqa: E402
+
+PAGE = 2 * 1024 * 1024
+OCCUPY_SRC = r"""
+extern "C" __global__ void occupy(unsigned long long ns, unsigned int *out) {
+    extern __shared__ unsigned int s[];
+    unsigned long long t0, t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    unsigned int n = 0;
+    do {
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        ++n;
+    } while (t - t0 < ns);
+    s[threadIdx.x] = n;
+    __syncthreads();
+    if (threadIdx.x == 0) out[blockIdx.x] = s[0];
+}
+"""
+
+
+@pytest.fixture(scope="module")
+def occupy():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    torch.cuda.set_device(0)
+    torch.zeros(1, device="cuda")  # the primary context is current
+    from cuda.bindings import driver as cu, nvrtc
+
+    err, prog = nvrtc.nvrtcCreateProgram(OCCUPY_SRC.encode(), b"occupy.cu", 0, [], [])
+    assert err == nvrtc.nvrtcResult.NVRTC_SUCCESS
+    opts = [b"--gpu-architecture=sm_100a"]
+    (err,) = nvrtc.nvrtcCompileProgram(prog, len(opts), opts)
+    if err != nvrtc.nvrtcResult.NVRTC_SUCCESS:
+        _, n = nvrtc.nvrtcGetProgramLogSize(prog)
+        log = b" " * n
+        nvrtc.nvrtcGetProgramLog(prog, log)
+        pytest.fail(log.decode(errors="replace"))
+    _, n = nvrtc.nvrtcGetCUBINSize(prog)
+    cubin = b" " * n
+    nvrtc.nvrtcGetCUBIN(prog, cubin)
+    err, mod = cu.cuModuleLoadData(cubin)
+    assert err == cu.CUresult.CUDA_SUCCESS
+    err, fn = cu.cuModuleGetFunction(mod, b"occupy")
+    assert err == cu.CUresult.CUDA_SUCCESS
+    smem = torch.cuda.get_device_properties(0).shared_memory_per_block_optin
+    (err,) = cu.cuFuncSetAttribute(fn, cu.CUfunction_attribute.CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, smem)
+    assert err == cu.CUresult.CUDA_SUCCESS
+    out = torch.zeros(64, dtype=torch.int32, device="cuda")
+
+    def launch(n_ctas, ns, stream):
+        args = ((ns, out.data_ptr()), (C.c_ulonglong, C.c_void_p))
+        (e,) = cu.cuLaunchKernel(fn, n_ctas, 1, 1, 1024, 1, 1, smem, cu.CUstream(stream.cuda_stream), args, 0)
+        assert e == cu.CUresult.CUDA_SUCCESS
+
+    yield launch
+    cu.cuModuleUnload(mod)
+
+
+def setup(M, N, dtype):
+    A_h = O.round_to(O.cfg_fill(M * N, 2, 0, O.NORMAL, 0.0, 0.02), dtype)
+    x_h = O.round_to(O.cfg_fill(N, 2, 1, O.NORMAL, 0.0, 1.0), dtype)
+    raw = torch.empty(A_h.nbytes + PAGE, dtype=torch.uint8, device="cuda")
+    off = (-raw.data_ptr()) % PAGE
+    A = raw[off: off + A_h.nbytes]
+    A.copy_(torch.from_numpy(A_h.view(np.int16)).cuda().view(torch.uint8).reshape(-1))
+    x = torch.from_numpy(x_h.view(np.int16)).cuda()
+    return raw, A, x, A_h, x_h
+
+
+@pytest.mark.parametrize("tma,placement,N", [
+    (True, None, 4096),         # ring kernels, whole rows
+    (True, "granules", 16384),  # ring kernels, granule split (exchange words)
+    (False, None, 4096),        # register kernels
+])
+def test_gemv_with_sms_held_by_other_work(occupy, tma, placement, N):
+    M, dt = 8192, L.F16
+    raw, A, x, A_h, x_h = setup(M, N, dt)
+    plan = L.GemvPlan(A, M, N, dt, L.F32, tma=tma, placement=placement)
+    modes = [L.MODE_AWARE, L.MODE_STREAM, L.MODE_SWAPPED, L.MODE_OBLIVIOUS]
+    s0 = torch.cuda.current_stream()
+    want = {}
+    for m in modes:
+        y = torch.empty(M, dtype=torch.float32, device="cuda")
+        plan.gemv(A, x, y, m, s0)
+        torch.cuda.synchronize()
+        want[m] = y.cpu().numpy()
+    before = plan.stats()["fallback_slots"]
+    s1 = torch.cuda.Stream()
+    ys = []
+    for rep in range(3):
+        occupy(8, 3_000_000, s1)  # 8 SMs held for 3 ms
+        for m in modes:
+            y = torch.full((M,), float("nan"), dtype=torch.float32, device="cuda")
+            plan.gemv(A, x, y, m, s0)
+            ys.append((m, y))
+        torch.cuda.synchronize()
+    st = plan.stats()
+    plan.close()
+    assert st["device_errors"] == 0
+    assert st["fallback_slots"] > before, "no CTA shared an SM: the helper did not hold any SM"
+    for m, y in ys:
+        assert np.array_equal(y.cpu().numpy(), want[m]), f"mode {m}"
+    ref = O.gemv_f64(A_h, x_h, dt, M, N, N)
+    assert O.rel_l2(ref, want[L.MODE_AWARE]) <= 2e-3
