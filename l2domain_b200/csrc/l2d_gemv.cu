@@ -93,12 +93,14 @@ struct GemvArgs {
     // rows [plo[g][k], phi[g][k]) (empty when equal), claimed pchunk[g][k] rows at a time from the
     // counter ctl[kCtlPool + 16 * pctr[g][k]].  psplit: stage-0 rows are split between the groups
     // by granule domain (dense AWARE / OBLIVIOUS / SWAPPED calls); every other row is whole.
-    int64_t plo[2][2], phi[2][2], pchunk[2][2];
-    int pctr[2][2];
+    // Stage 2, the tail, is claimed half a row at a time (pchunk 1 = one half): the last claims of a
+    // call stay small, and a row's two halves meet in its exchange word like a split row's parts.
+    int64_t plo[2][3], phi[2][3], pchunk[2][3];
+    int pctr[2][3];
     int psplit;
     int pool_parity;              // ring kernels: the pool counters and slot flags of this launch (launches mod 2)
     unsigned long long call_no;   // this call's number on the plan (1, 2, ...; from the host): its exchange tag
-    int64_t ctr_base[3];          // ring kernels: chunk index of counter value 0 (the static first chunks come before)
+    int64_t ctr_base[4];          // ring kernels: chunk index of counter value 0 (the static first chunks come before)
     unsigned long long *rflag;    // ring kernels: [2][n_slots] call number that last took each SM slot's first chunks
     int first_chunks[2];          // ring kernels: chunks in the first claim of a group-g CTA (group 0: unsplit)
     // Sided matrices (l2d_sided_*): rows [0, sided_r0) live in granules homed in domain 0, the rest
@@ -740,16 +742,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 // are claimed a chunk at a time from one counter per pool, so a domain group's SMs finish together
 // whatever bandwidth each one gets.
 constexpr int kCtlEpoch = 0, kCtlDone = 1, kCtlFallback = 2, kCtlError = 3;
-// ctl[kCtlPool + 16 (3 p + c)]: pool counter c (0, 1, 2) of launches of parity p.  A ring launch
+// ctl[kCtlPool + 16 (4 p + c)]: pool counter c (0-3) of launches of parity p.  A ring launch
 // claims rows before the previous launch on the stream has completed (programmatic dependent
 // launch), so consecutive launches use different counters; the previous launch zeroed these once
 // the launch two back, which used them, had completed (ring_call).  ctl[kCtlDone]: the register
 // kernels' count of finished CTAs.
 constexpr int kCtlPool = 16;
-constexpr int kCtlWords = kCtlPool + 16 * 6;
+constexpr int kCtlWords = kCtlPool + 16 * 8;
 
 __device__ __forceinline__ unsigned long long *pool_counter(const GemvArgs &a, int pool, int grp) {
-    return a.ctl + kCtlPool + 16 * (3 * a.pool_parity + a.pctr[grp][pool]);
+    return a.ctl + kCtlPool + 16 * (4 * a.pool_parity + a.pctr[grp][pool]);
 }
 
 // Granule j of row `row` of a sided matrix.  Rows of side s = (row >= sided_r0) use the granules of
@@ -783,8 +785,9 @@ template <bool SPLIT> struct PoolWalker {
     unsigned long long nxt; // lane 0: the claim in flight for the chunk after this one
     bool nxt_valid;
     bool nxt_raw;           // nxt is a counter value (chunk ctr_base + nxt), not a chunk index
-    int pool;               // stage of the group's pool table being walked (2: nothing left)
+    int pool;               // stage of the group's pool table being walked (3: nothing left)
     int grp, G;
+    int half;               // tail stage: 1 / 2 = the first / second half of the row, 0 = not a half
     uint32_t mask;          // granules of the current row still to fetch
     bool whole;
     const uint8_t *rowp;
@@ -793,7 +796,8 @@ template <bool SPLIT> struct PoolWalker {
     __device__ __forceinline__ void start(const GemvArgs &a, int grp_, long long k_first, long long k_second) {
         grp = grp_;
         G = static_cast<int>(a.row_bytes >> kGranShift);
-        pool = a.plo[grp][0] < a.phi[grp][0] ? 0 : 1;
+        pool = a.plo[grp][0] < a.phi[grp][0] ? 0 : a.plo[grp][1] < a.phi[grp][1] ? 1 : 2;
+        half = 0;
         row = end = 0;
         k2 = k_second;
         nxt = static_cast<unsigned long long>(k_first);
@@ -808,7 +812,7 @@ template <bool SPLIT> struct PoolWalker {
     // The next chunk: a chunk of the first claim, the claim in flight, or a new one; when a pool
     // runs dry the walk moves to the group's next stage.
     __device__ __forceinline__ bool take_chunk(const GemvArgs &a, int lane) {
-        while (pool < 2) {
+        while (pool < 3) {
             unsigned long long v = nxt;
             bool raw = nxt_raw;
             if (!nxt_valid) {
@@ -819,10 +823,11 @@ template <bool SPLIT> struct PoolWalker {
             if (raw) k += a.ctr_base[a.pctr[grp][pool]];
             nxt_valid = false;
             const int64_t lo = a.plo[grp][pool], hi = a.phi[grp][pool], c = a.pchunk[grp][pool];
-            const int64_t r = lo + k * c;
+            const int64_t r = pool == 2 ? lo + (k >> 1) : lo + k * c;
             if (r < hi) {
                 row = r;
-                end = min(r + c, hi);
+                end = pool == 2 ? r + 1 : min(r + c, hi);
+                half = pool == 2 ? 1 + static_cast<int>(k & 1) : 0;
                 if (k2 >= 0) {
                     nxt = static_cast<unsigned long long>(k2);
                     nxt_valid = true;
@@ -842,9 +847,9 @@ template <bool SPLIT> struct PoolWalker {
     // for long -- when a pool runs dry, every warp has at most the rest of one chunk left.
     __device__ __forceinline__ void claim_ahead(const GemvArgs &a, int lane) {
 #if L2D_CLAIM_EARLY
-        if (nxt_valid || pool >= 2 || row + 1 < end) return;  // with the first copy of the chunk's last row
+        if (nxt_valid || pool >= 3 || row + 1 < end) return;  // with the first copy of the chunk's last row
 #else
-        if (nxt_valid || pool >= 2 || mask != 0u || row + 1 < end) return;
+        if (nxt_valid || pool >= 3 || mask != 0u || row + 1 < end) return;
 #endif
         if (lane == 0) nxt = atomicAdd(pool_counter(a, pool, grp), 1ull);
         nxt_valid = true;
@@ -869,8 +874,9 @@ template <bool SPLIT> struct PoolWalker {
                                    (a.row_place ? 0ull : static_cast<uint64_t>(lane) << (kGranShift - kUnitShift));
                 own = (a.row_place ? row_owner<true>(a, row, u) : unit_dom<true>(a, u)) == grp;
             }
+            if (half) own = own && (lane >= (half - 1) * (G >> 1)) && (lane < half * (G >> 1));
             mask = __ballot_sync(0xffffffffu, own);
-            whole = !split_row || mask == (G == 32 ? 0xffffffffu : (1u << G) - 1u);
+            whole = half == 0 && (!split_row || mask == (G == 32 ? 0xffffffffu : (1u << G) - 1u));
             if (mask == 0u) ++row;  // every granule is the other group's: the row is whole there
         }
         const int g = __ffs(mask) - 1;
@@ -1075,7 +1081,7 @@ __device__ __forceinline__ bool walk_pools(const GemvArgs &a, int grp, long long
             for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
             if (lane == 0) {
                 const int64_t row = m.row;
-                if (!SPLIT || (m.last & 2)) {
+                if (m.last & 2) {
                     store_out<DT_OUT>(a.y + ring_y_index(a, row) * eo, sum);
                     final_to_peers<DT_OUT, SH>(a, row, sum);
                 } else {
@@ -1173,7 +1179,7 @@ __device__ __forceinline__ void ring_call(const GemvArgs &a, uint8_t *smem) {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");  // A, x and y may belong to the previous kernel
     if (blockIdx.x == 0 && tid == 0)
-        for (int c = 0; c < 3; ++c) a.ctl[kCtlPool + 16 * (3 * (a.pool_parity ^ 1) + c)] = 0ull;
+        for (int c = 0; c < 4; ++c) a.ctl[kCtlPool + 16 * (4 * (a.pool_parity ^ 1) + c)] = 0ull;
     stage_x_start<SH>(a, smem);
     __syncthreads();
     const long long k0 = slot >= 0 && first > 0 ? static_cast<long long>(slot) * first : -1;
@@ -1763,8 +1769,12 @@ bool use_ring(const l2d_plan *p, bool split) {
 #ifndef L2D_SPLIT_CHUNK_SHARE
 #define L2D_SPLIT_CHUNK_SHARE 0  // 1: split-pool chunks sized on the group's half of each row
 #endif
+#ifndef L2D_TAIL
+#define L2D_TAIL 1  // 0: no tail stage (the A/B control)
+#endif
 struct RingPools {
     int64_t whole_lo = 0;    // rows [whole_lo, rows_total) are the whole pool
+    int64_t tail_lo = 0;     // rows [tail_lo, rows_total) of it, the tail, are claimed half a row at a time
     int64_t chunk = 1;       // rows per claim from the whole pool
     int64_t chunk_split = 1; // rows per claim from a split pool
     int first[2] = {0, 0};   // chunks of each group's CTAs' first claim (group 0's for unsplit calls)
@@ -1817,7 +1827,16 @@ RingPools ring_pools(const l2d_plan *p, bool split, int mode) {
             rp.whole_lo = R - whole;
         }
     }
-    const int64_t pool_rows = split ? rp.whole_lo : R;
+    // The tail: when the pools before it run dry, a warp holds at most one chunk (a 32 KiB row or
+    // more) and the call ends with the slowest of those; half-row claims after them halve what is
+    // left to the last warps.  One row per warp of the grid, at most the whole pool, on rows of
+    // 8-32 granules (even) when the call has at least four rows per warp.  Measured on the 512 MiB
+    // shard: 77.6 -> 77.3 us AWARE, 77.7 -> 76.8 us STREAM; a tail of two rows per warp was no better.
+    const int64_t G = rb >> kGranShift;
+    rp.tail_lo = R;
+    if (L2D_TAIL && G >= 8 && !(G & 1) && (rb & (kGranBytes - 1)) == 0 && R >= 4 * warps)
+        rp.tail_lo = R - std::min<int64_t>(warps, R - rp.whole_lo);
+    const int64_t pool_rows = split ? rp.whole_lo : rp.tail_lo;
     const int64_t c = split ? rp.chunk_split : rp.chunk;
     const int64_t chunks = (pool_rows + c - 1) / c;
     for (int g = 0; g < 2; ++g) rp.first[g] = first_chunks_of(chunks, n_ctas[g]);
@@ -1827,7 +1846,7 @@ RingPools ring_pools(const l2d_plan *p, bool split, int mode) {
 // Counter bases: the chunks of a pool before n_g F (F = first_chunks[g]) are the static first chunks
 // of the n_g CTAs of the group that starts on that pool; the pool's counter hands out the rest.
 void set_counter_bases(const l2d_plan *p, bool split, GemvArgs *a) {
-    a->ctr_base[0] = a->ctr_base[1] = a->ctr_base[2] = 0;
+    a->ctr_base[0] = a->ctr_base[1] = a->ctr_base[2] = a->ctr_base[3] = 0;
     for (int g = 0; g < (split ? 2 : 1); ++g) {
         const int F = a->first_chunks[g];
         if (F <= 0) continue;
@@ -1884,15 +1903,20 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     a.xch = p->d_xch;
     const RingPools rp = ring_pools(p, split, mode);
     for (int g = 0; g < 2; ++g) {
-        // stage 0: the group's split pool (split calls), stage 1: the whole pool shared by both
+        // stage 0: the group's split pool (split calls), stage 1: the whole pool shared by both,
+        // stage 2: its tail, in half rows
         a.plo[g][0] = 0;
         a.phi[g][0] = split ? rp.whole_lo : 0;
         a.pchunk[g][0] = rp.chunk_split;
         a.pctr[g][0] = g;
         a.plo[g][1] = split ? rp.whole_lo : 0;
-        a.phi[g][1] = p->rows_total;
+        a.phi[g][1] = rp.tail_lo;
         a.pchunk[g][1] = rp.chunk;
         a.pctr[g][1] = 2;
+        a.plo[g][2] = rp.tail_lo;
+        a.phi[g][2] = p->rows_total;
+        a.pchunk[g][2] = 1;
+        a.pctr[g][2] = 3;
     }
     a.psplit = split ? 1 : 0;
     a.pool_parity = static_cast<int>(p->ring_launches & 1ull);
@@ -1919,13 +1943,16 @@ int build_args(l2d_plan *p, const void *A, const void *x, void *y, int mode, Gem
     return L2D_OK;
 }
 
-// Every stage of the pool table inside [0, rows_total) with a positive chunk and a counter 0-2.
+// Every stage of the pool table inside [0, rows_total) with a positive chunk and a counter 0-3; a
+// tail stage only for rows of an even number of granules.
 bool pools_valid(const GemvArgs &a) {
-    for (int g = 0; g < 2; ++g)
-        for (int k = 0; k < 2; ++k)
+    for (int g = 0; g < 2; ++g) {
+        for (int k = 0; k < 3; ++k)
             if (a.plo[g][k] < 0 || a.phi[g][k] < a.plo[g][k] || a.phi[g][k] > a.rows_total || a.pchunk[g][k] <= 0 ||
-                a.pctr[g][k] < 0 || a.pctr[g][k] > 2)
+                a.pctr[g][k] < 0 || a.pctr[g][k] > 3)
                 return false;
+        if (a.phi[g][2] > a.plo[g][2] && ((a.row_bytes >> kGranShift) & 1)) return false;
+    }
     return true;
 }
 
@@ -2137,6 +2164,10 @@ int sided_args(l2d_sided *s, const void *x, void *y, int mode, GemvArgs *a, bool
     a->sided = 1;
     a->sided_r0 = s->r0;
     a->psplit = 0;
+    for (int g = 0; g < 2; ++g) {  // no tail stage: its rows go back to the stage before it
+        if (a->phi[g][2] > a->plo[g][2]) a->phi[g][1] = a->phi[g][2];
+        a->plo[g][2] = a->phi[g][2] = 0;
+    }
     return L2D_OK;
 }
 

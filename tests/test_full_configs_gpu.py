@@ -13,7 +13,8 @@ max |y - y_cpu| <= 1e-3 against its sequential fp32 check loop
 * Configs 4 and 5 (4 GiB each) are generated on the device by l2d_fill_cfg; the rows checked are
   regenerated on the host by the oracle, asserted bit-identical to the device's bytes, and the
   oracle's y of those rows is the reference.  Config 4: the first and last 256 rows of every one
-  of the 32 problems plus two whole problems.  Config 5: rows at the start, the middle and the end,
+  of the 32 problems plus two whole problems.  Config 5: rows at the start, the middle and the end
+  (the last 2560, which hold the ring kernels' tail of half-row claims),
   once with A on a 2 MiB boundary and once 4 KiB past one, where every 64th 32 KiB row straddles two
   2 MiB pages (all of those rows are checked).
 """
@@ -189,7 +190,8 @@ def test_cfg5_4gib_sampled_rows(kernels, offset):
     out, ring_modes = run_modes(A, x, M, N, dt, 1, tma)
     if kernels == "default":
         assert ring_modes == 0b1111
-    rows = [np.arange(0, 256), np.arange(M // 2 - 128, M // 2 + 128), np.arange(M - 256, M)]
+    # the end: the last 2560 rows cover the ring kernels' tail (rows claimed half a row at a time)
+    rows = [np.arange(0, 256), np.arange(M // 2 - 128, M // 2 + 128), np.arange(M - 2560, M)]
     if offset:
         row_bytes = N * 2
         start = offset + np.arange(M, dtype=np.int64) * row_bytes

@@ -5,7 +5,8 @@ applied to the GEMV's A.
   holds that part of the dense row, byte for byte.
 * Results: every mode against the fp64 oracle (fp32 relative L2 <= 1e-5, fp16/bf16 <= 2e-3 of the
   same rounded inputs, rounded to the output type); since each row is one warp's, granules in order,
-  all modes give the same bits, equal to the dense plan's STREAM call on the same A.
+  all modes give the same bits, equal to the dense plan's STREAM call on the same A (these shapes
+  are below the size from which a dense call sums its last rows in halves).
 """
 import numpy as np
 import pytest
