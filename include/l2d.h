@@ -261,7 +261,8 @@ L2D_API int l2d_plan_domain_map(const l2d_plan *plan, int *sm_domain, int cap, i
  * l2d_probe_addr_domains output; map may be NULL for STREAM).  Each call launches a one-CTA
  * set-up kernel that receives the call's SM->slot table and attr bits as kernel parameters, then
  * the GEMV kernel; nothing is copied from host memory.  The first call on a device looks up the
- * array's address and clears it, and waits for that to finish; later calls only enqueue work.
+ * array's address (cudaGetSymbolAddress) and clears it, and waits for that to finish; later calls
+ * only enqueue work.  Make that first call on each device before any stream capture begins.
  * Calls share the array and each leaves its contents for the next: calls that overlap on the GPU
  * (other streams, other threads) race and must be serialised by the caller.  Sizes beyond the
  * limits below return L2D_ERR_INVALID. */

@@ -2374,7 +2374,8 @@ std::mutex g_mu;
 uint8_t *g_ptr[kMaxDevices] = {nullptr};
 
 // First call on a device: the device address of g_scratch (host code may not use the symbol
-// itself as a pointer) and one clear of the whole array.  Runs with `device` current.
+// itself as a pointer) and one clear of the whole array, waited for.  Runs with `device` current;
+// callers make this first call before any stream capture begins.
 int setup(int device, uint8_t **out) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_ptr[device]) {
