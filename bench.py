@@ -314,9 +314,10 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
     def gbs(nbytes, us):
         return {k: round(nbytes / (v * 1e-6) / 1e9, 1) for k, v in us.items() if v}
 
-    def sided_us(A, x, y, M, N, dt, calls):
-        """The same matrix packed by L2 domain (l2d_sided_*): µs per call of each mode."""
-        s = L.SidedMatrix(M, N, dt, dt, device=local)
+    def sided_us(A, x, y, M, N, dt, calls, pooled=False):
+        """The same matrix packed by L2 domain (l2d_sided_*; pooled: on pages of the domain-classified
+        pool, l2d_sided_create_pooled): µs per call of each mode."""
+        s = L.SidedMatrix(M, N, dt, dt, device=local, pooled=pooled)
         s.pack(A, stream=stream)
         res = {name: round(kernel_time_us(lambda m=mode: s.gemv(x, y, m, stream), calls, stream), 3)
                for name, mode in (("aware", 1), ("swapped", 2), ("stream", 3))}
@@ -354,6 +355,7 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                    "frac_of_l2_read_peak": {k: round(v / l2_peak, 4) for k, v in g.items()},
                    "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 200, 20, 0),
                    "sided_us": sided_us(A, x, y, M, N, dt, 1000),
+                   "sided_pool_us": sided_us(A, x, y, M, N, dt, 1000, pooled=True),
                    "placements": other_placement(plan, A, x, y, M, N, dt, 1000)}
     plan.close()
     del raw, A
@@ -371,6 +373,7 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                         "aware_speedup_vs_oblivious": round(us["oblivious"] / us["aware"], 4),
                         "swapped_slowdown_vs_aware": round(us["swapped"] / us["aware"], 4),
                         "sided_us": sided_us(A, x, y, M, N, dt, 500),
+                   "sided_pool_us": sided_us(A, x, y, M, N, dt, 500, pooled=True),
                         "placements": other_placement(plan, A, x, y, M, N, dt, 500)}
     plan.close()
     del raw, A
@@ -414,9 +417,12 @@ def side_configs(L, torch, dev, local, stream, copy_peak, read_peak):
                    "frac_of_copy_peak": {k: round(v / copy_peak, 4) for k, v in g.items()},
                    "cublas_cli_us_per_event_pair": cublas_cli_us(M, N, dt, 20, 5, 0),
                    "sided_us": sided_us(A, x, y, M, N, dt, 50),
+                   "sided_pool_us": sided_us(A, x, y, M, N, dt, 50, pooled=True),
                    "placements": other_placement(plan, A, x, y, M, N, dt, 50)}
     plan.close()
     del raw, A
+
+    L.pool_release(local)  # the pooled sided matrices are gone: unmap the pool's chunks
 
     # Config 4: batched fp16 32 x (8192x8192) (4 GiB), 10 back-to-back calls.
     B, M, N, dt = 32, 8192, 8192, F16

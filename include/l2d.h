@@ -282,8 +282,9 @@ L2D_API int l2d_gemv_noalloc(const l2d_gemv_desc *desc, const l2d_domain_map *ma
  * partials -- and a group that finishes first takes over the other side's remaining rows; SWAPPED
  * starts every group on the far side (the control); STREAM (and OBLIVIOUS, the same for whole rows)
  * hands rows to any SM.  Every mode computes each row in one warp with its granules in order, so
- * all modes give the same bits, equal to l2d_gemv's STREAM on the dense A.  Rows must be whole 4 KiB
- * granules, at most 96 KiB (x is staged in shared memory); one problem. */
+ * all modes give the same bits, equal to l2d_gemv's STREAM on the dense A (except on the last rows
+ * of a large dense call on rows of 8+ granules, which l2d_gemv sums in two halves).  Rows must be
+ * whole 4 KiB granules, at most 96 KiB (x is staged in shared memory); one problem. */
 typedef struct l2d_sided l2d_sided;
 typedef struct {
     int64_t rows_side[2];   /* rows stored in domain-0 and domain-1 granules */
@@ -295,6 +296,13 @@ typedef struct {
 /* desc: M, N, dtype_in, dtype_out, device (lda, strides, A and flags are ignored; batch <= 1).
  * Allocates the buffer and probes its pages' domains (and the SM map unless it is cached). */
 L2D_API int l2d_sided_create(const l2d_gemv_desc *desc, l2d_sided **out);
+/* The same with the buffer taken from the device's domain-classified pool (l2d_pool_*, the role of
+ * cudaMallocSided, utility/sidedgpu.cu:791-838): a run of whole free 2 MiB pages (the pool grows
+ * 1 GiB at a time as needed; opts tunes the probes of new chunks, NULL = defaults), each side's rows
+ * then in granules the pool classified as that side -- checked granule by granule at creation
+ * (L2D_ERR_PROBE_AMBIGUOUS if the pool and the layout disagree).  l2d_sided_destroy returns the
+ * pages to the pool. */
+L2D_API int l2d_sided_create_pooled(const l2d_gemv_desc *desc, const l2d_probe_opts *opts, l2d_sided **out);
 /* Copies the dense row-major A (lda elements per row, 0 = N) into the sided layout, stream-ordered. */
 L2D_API int l2d_sided_pack(l2d_sided *s, const void *A, int64_t lda, void *stream);
 L2D_API int l2d_gemv_sided(l2d_sided *s, const void *x, void *y, int mode, void *stream);

@@ -126,6 +126,7 @@ SIGNATURES = {
     "l2d_plan_domain_map": (_i, [_vp, _pi, _i, _pi, _pu32]),
     "l2d_gemv_noalloc": (_i, [C.POINTER(GemvDesc), C.POINTER(DomainMap), _vp, _vp, _i, _vp]),
     "l2d_sided_create": (_i, [C.POINTER(GemvDesc), C.POINTER(_vp)]),
+    "l2d_sided_create_pooled": (_i, [C.POINTER(GemvDesc), C.POINTER(ProbeOpts), C.POINTER(_vp)]),
     "l2d_sided_pack": (_i, [_vp, _vp, _i64, _vp]),
     "l2d_gemv_sided": (_i, [_vp, _vp, _vp, _i, _vp]),
     "l2d_sided_info": (_i, [_vp, _vp]),
@@ -430,14 +431,20 @@ class SidedMatrix:
     """A copy of a dense row-major M x N matrix placed by L2 domain (the cudaMallocSided placement of
     utility/sidedgpu.cu:791-838 applied to the GEMV's A): the first rows_side[0] rows live only in
     granules homed in domain 0, the rest only in domain-1 granules.  ``pack(A)`` copies A in;
-    ``gemv(x, y, mode)`` computes y = A.x, in AWARE mode from near granules only."""
+    ``gemv(x, y, mode)`` computes y = A.x, in AWARE mode from near granules only.  ``pooled=True``
+    takes the buffer as whole pages of the device's domain-classified pool (l2d_pool_*) instead of
+    a buffer of its own."""
 
-    def __init__(self, M: int, N: int, dtype_in: int = F16, dtype_out: Optional[int] = None, device: int = 0):
+    def __init__(self, M: int, N: int, dtype_in: int = F16, dtype_out: Optional[int] = None, device: int = 0,
+                 pooled: bool = False):
         self._s = C.c_void_p(0)
         self.M, self.N, self.device = M, N, device
         desc = GemvDesc(M=M, N=N, lda=0, dtype_in=dtype_in, dtype_out=dtype_in if dtype_out is None else dtype_out,
                         batch=1, stride_a=0, stride_x=0, stride_y=0, device=device, A=None, flags=0)
-        check(lib().l2d_sided_create(C.byref(desc), C.byref(self._s)))
+        if pooled:
+            check(lib().l2d_sided_create_pooled(C.byref(desc), None, C.byref(self._s)))
+        else:
+            check(lib().l2d_sided_create(C.byref(desc), C.byref(self._s)))
 
     def pack(self, A, lda: int = 0, stream=None) -> None:
         check(lib().l2d_sided_pack(self._s, _ptr(A), lda, _stream_handle(stream)))

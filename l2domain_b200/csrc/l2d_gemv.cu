@@ -2130,6 +2130,7 @@ struct l2d_sided {
     void *raw = nullptr;
     uint8_t *base = nullptr;  // 2 MiB aligned
     size_t bytes = 0;
+    uint64_t pool_first = 0, pool_granules = 0;  // pooled: granules [pool_first, +pool_granules) of the device's pool
     uint32_t mask = 0;
     std::vector<int> attr;    // per 2 MiB page of [base, base + bytes)
     l2d_plan *plan = nullptr; // over the buffer: scratch, domain map and kernel choice of the calls
@@ -2148,10 +2149,23 @@ struct DeviceScope {
     }
 };
 
+int sided_create(const l2d_gemv_desc *desc, bool pooled, const l2d_probe_opts *opts, l2d_sided **out);
+
+// Gives a pooled sided matrix's pages back to the device's pool.
+int sided_pool_release(l2d_sided *s) {
+    if (!s->pool_granules) return L2D_OK;
+    std::vector<uint64_t> g(static_cast<size_t>(s->pool_granules));
+    for (size_t k = 0; k < g.size(); ++k) g[k] = s->pool_first + k;
+    const int st = l2d_pool_free(s->device, g.data(), g.size());
+    s->pool_granules = 0;
+    return st;
+}
+
 int sided_fail(l2d_sided *s, int st) {
     if (s) {
         if (s->plan) l2d_plan_destroy(s->plan);
         if (s->raw) cudaFree(s->raw);
+        sided_pool_release(s);
         delete s;
     }
     return st;
@@ -2176,6 +2190,19 @@ int sided_args(l2d_sided *s, const void *x, void *y, int mode, GemvArgs *a, bool
 extern "C" {
 
 int l2d_sided_create(const l2d_gemv_desc *desc, l2d_sided **out) {
+    return sided_create(desc, false, nullptr, out);
+}
+
+int l2d_sided_create_pooled(const l2d_gemv_desc *desc, const l2d_probe_opts *opts, l2d_sided **out) {
+    return sided_create(desc, true, opts, out);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Storage: cudaMalloc (own buffer) or whole pages of the device's domain-classified pool.
+int sided_create(const l2d_gemv_desc *desc, bool pooled, const l2d_probe_opts *opts, l2d_sided **out) {
     clear_error();
     if (!desc || !out) return set_error(L2D_ERR_INVALID, "sided_create: null argument");
     *out = nullptr;
@@ -2202,11 +2229,22 @@ int l2d_sided_create(const l2d_gemv_desc *desc, l2d_sided **out) {
     const int64_t per_side = std::max(s->r0, d.M - s->r0) * s->G;  // granules each side needs
     const int64_t pages = (per_side + 255) / 256;
     s->bytes = static_cast<size_t>(pages) * kPageBytes;
-    cudaError_t e = cudaMalloc(&s->raw, s->bytes + kPageBytes);
-    if (e != cudaSuccess) return sided_fail(s, set_error(L2D_ERR_CUDA, "sided buffer: %s", cudaGetErrorString(e)));
-    s->base = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(s->raw) + kPageBytes - 1) & ~(kPageBytes - 1));
-    e = cudaMemset(s->raw, 0, s->bytes + kPageBytes);
-    if (e != cudaSuccess) return sided_fail(s, set_error(L2D_ERR_CUDA, "sided buffer: %s", cudaGetErrorString(e)));
+    if (pooled) {
+        void *pool_base = nullptr;
+        int pst = pool_take_pages(d.device, static_cast<size_t>(pages), opts, &s->pool_first, &pool_base);
+        if (pst != L2D_OK) return sided_fail(s, pst);
+        s->pool_granules = static_cast<uint64_t>(pages) * (kPageBytes / kGranBytes);
+        s->base = static_cast<uint8_t *>(pool_base) + s->pool_first * kGranBytes;
+        cudaError_t e = cudaMemset(s->base, 0, s->bytes);
+        if (e != cudaSuccess) return sided_fail(s, set_error(L2D_ERR_CUDA, "sided buffer: %s", cudaGetErrorString(e)));
+    } else {
+        cudaError_t e = cudaMalloc(&s->raw, s->bytes + kPageBytes);
+        if (e != cudaSuccess) return sided_fail(s, set_error(L2D_ERR_CUDA, "sided buffer: %s", cudaGetErrorString(e)));
+        s->base =
+            reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(s->raw) + kPageBytes - 1) & ~(kPageBytes - 1));
+        e = cudaMemset(s->raw, 0, s->bytes + kPageBytes);
+        if (e != cudaSuccess) return sided_fail(s, set_error(L2D_ERR_CUDA, "sided buffer: %s", cudaGetErrorString(e)));
+    }
     std::vector<int> sm;
     int st = cached_sm_map(d.device, sm);
     if (st != L2D_OK) return sided_fail(s, st);
@@ -2229,9 +2267,38 @@ int l2d_sided_create(const l2d_gemv_desc *desc, l2d_sided **out) {
     if (st != L2D_OK) return sided_fail(s, st);
     if (!s->plan->tma)
         return sided_fail(s, set_error(L2D_ERR_UNSUPPORTED, "sided matrices run on the granule-ring kernels only"));
+    if (pooled) {
+        // The layout puts side s's rows only in granules the pool classified as side s: check every one.
+        const int64_t per_row = s->G;
+        std::vector<uint64_t> g;
+        std::vector<int> want;
+        g.reserve(static_cast<size_t>(d.M * per_row));
+        for (int64_t r = 0; r < d.M; ++r) {
+            std::vector<uint64_t> addr(static_cast<size_t>(per_row));
+            int n = 0;
+            st = l2d_sided_row_granules(s, r, addr.data(), static_cast<int>(per_row), &n);
+            if (st != L2D_OK) return sided_fail(s, st);
+            for (int j = 0; j < n; ++j) {
+                g.push_back((addr[j] - reinterpret_cast<uint64_t>(s->base)) / kGranBytes + s->pool_first);
+                want.push_back(r >= s->r0 ? 1 : 0);
+            }
+        }
+        std::vector<int> side(g.size(), -1);
+        st = l2d_pool_side(d.device, g.data(), g.size(), side.data());
+        if (st != L2D_OK) return sided_fail(s, st);
+        for (size_t k = 0; k < g.size(); ++k)
+            if (side[k] != want[k])
+                return sided_fail(s, set_error(L2D_ERR_PROBE_AMBIGUOUS,
+                                               "pool granule %llu is classified side %d, the layout needs side %d",
+                                               static_cast<unsigned long long>(g[k]), side[k], want[k]));
+    }
     *out = s;
     return L2D_OK;
 }
+
+}  // namespace
+
+extern "C" {
 
 int l2d_sided_pack(l2d_sided *s, const void *A, int64_t lda, void *stream) {
     clear_error();
@@ -2316,7 +2383,9 @@ int l2d_sided_destroy(l2d_sided *s) {
     DeviceScope scope(s->device);
     int st = s->plan ? l2d_plan_destroy(s->plan) : L2D_OK;
     cudaError_t e = s->raw ? cudaFree(s->raw) : cudaSuccess;
+    const int pst = sided_pool_release(s);
     delete s;
+    if (st == L2D_OK) st = pst;
     if (st != L2D_OK) return st;
     if (e != cudaSuccess) return set_error(L2D_ERR_CUDA, "sided_destroy: %s", cudaGetErrorString(e));
     return L2D_OK;

@@ -36,6 +36,9 @@ inline int lowest_bit_or(uint32_t mask, int fallback) { return mask ? __builtin_
 // SM -> domain map of a device, once per process: read from the domain-map cache when
 // $SIDEDGPU_CONFIG_DIR holds one keyed to the device, probed otherwise (l2d_gemv.cu).
 int cached_sm_map(int device, std::vector<int> &out, bool *from_file = nullptr);
+// l2d_pool.cu: a run of whole free 2 MiB pages of the device's pool (every granule marked used);
+// granule indices [*first, *first + pages * 512) from *base.
+int pool_take_pages(int device, size_t pages, const l2d_probe_opts *opts, uint64_t *first, void **base);
 
 // Peer-memory sharding fields of one l2d_gemv_sharded step (device pointers unless noted).
 struct ShardArgs {

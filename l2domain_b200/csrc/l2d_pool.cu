@@ -175,6 +175,46 @@ int grow(Pool &p, int device, const l2d_probe_opts *opts) {
 
 using namespace l2d;
 
+namespace l2d {
+
+// Whole 2 MiB pages for a sided matrix (l2d_sided_create_pooled): the lowest run of `pages` pages
+// of the pool none of whose granules is handed out, the pool grown by chunks until one exists.
+// Every granule of the run is marked used (a sided matrix uses both domains' granules of each
+// page: one side's rows in one, the other side's in the other); they go back with l2d_pool_free.
+int pool_take_pages(int device, size_t pages, const l2d_probe_opts *opts, uint64_t *first, void **base) {
+    if (!first || !base || pages == 0) return set_error(L2D_ERR_INVALID, "pool_take_pages: bad argument");
+    const uint64_t per_page = (uint64_t(1) << kPageShift) / pool::kGranule;
+    if (pages * per_page * pool::kGranule > pool::kReserve)
+        return set_error(L2D_ERR_INVALID, "pool_take_pages: %zu pages exceed the pool's 64 GiB", pages);
+    int st = pool::check_device(device);
+    if (st != L2D_OK) return st;
+    pool::Pool &p = pool::g_pools[device];
+    std::lock_guard<std::mutex> lk(p.mu);
+    pool::DeviceScope scope(device);
+    for (;;) {
+        uint64_t run = 0;
+        for (uint64_t g = 0; g + per_page <= p.used.size(); g += per_page) {
+            bool page_free = true;
+            for (uint64_t k = 0; k < per_page && page_free; ++k) page_free = !p.used[g + k];
+            run = page_free ? run + 1 : 0;
+            if (run == pages) {
+                const uint64_t g0 = g + per_page - run * per_page;
+                for (uint64_t k = g0; k < g0 + run * per_page; ++k) {
+                    p.used[k] = 1;
+                    --p.free_count[p.side[k]];
+                }
+                *first = g0;
+                *base = reinterpret_cast<void *>(p.base);
+                return L2D_OK;
+            }
+        }
+        st = pool::grow(p, device, opts);
+        if (st != L2D_OK) return st;
+    }
+}
+
+}  // namespace l2d
+
 extern "C" {
 
 int l2d_pool_alloc(int device, size_t bytes, int side, const l2d_probe_opts *opts, uint64_t *granules, size_t cap,

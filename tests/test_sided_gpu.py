@@ -117,3 +117,40 @@ def test_sided_rejects_rows_off_granules():
     with pytest.raises(L.L2DError) as e:
         L.SidedMatrix(100, 2048, L.F16, device=0).gemv(None, None, 9)
     assert e.value.status == -1
+
+
+@pytest.mark.parametrize("M,N,dt,do", [
+    (3000, 4096, L.F16, L.F16),    # 8 KiB rows
+    (513, 16384, L.F16, L.F32),    # 32 KiB rows
+])
+def test_pooled_sided_matrix_matches_oracle_and_dense_stream(M, N, dt, do):
+    """A sided matrix on whole pages of the domain-classified pool (l2d_sided_create_pooled): the
+    buffer lies inside the pool, its granules are marked used while it lives and free again after
+    l2d_sided_destroy, and every mode gives the oracle's values and the dense STREAM call's bits."""
+    raw, A, x, A_h, x_h = dense(M, N, dt)
+    free0 = None
+    s = L.SidedMatrix(M, N, dt, do, pooled=True)
+    plan = L.GemvPlan(A, M, N, dt, do, tma=True)
+    try:
+        info = s.info()
+        pool_base, pinfo = L.get_sided_pool_base(0), L.pool_info(0)
+        assert pool_base <= info["base"] and info["base"] + info["bytes"] <= pool_base + pinfo["mapped_bytes"]
+        free0 = sum(pinfo["free_granules"])
+        s.pack(A)
+        y64 = O.gemv_f64(A_h, x_h, dt, M, N)
+        ref = (O.round_out(y64, do) if do != L.F32 else y64).astype(np.float64)
+        y_dense = torch.full((M,), -1, dtype=TSTORE[do], device="cuda")
+        plan.gemv(A, x, y_dense, L.MODE_STREAM)
+        for mode in MODES:
+            y = torch.full((M,), -1, dtype=TSTORE[do], device="cuda")
+            s.gemv(x, y, mode)
+            torch.cuda.synchronize()
+            h = y.cpu().numpy()
+            got = h if do == L.F32 else O.widen(h.view(np.uint16), do)
+            assert O.rel_l2(ref, got) <= TOL[dt], f"mode {mode}"
+            assert torch.equal(y, y_dense), f"mode {mode} differs from the dense STREAM call"
+    finally:
+        s.close()
+        plan.close()
+    assert sum(L.pool_info(0)["free_granules"]) == free0 + info["bytes"] // 4096
+    L.pool_release(0)  # every granule is free again: the pool unmaps its chunks
