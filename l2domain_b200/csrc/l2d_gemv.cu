@@ -20,14 +20,19 @@
 //    cut into the intervals where one slot of each group overlaps; the second of the two slots to
 //    finish an interval adds part[0] + part[1] for all its rows (commutative, so deterministic)
 //    and stores y, coalesced.  No second kernel.
-//  * Rows are blocked per slot (one slot per SM) and interleaved over the CTA's warps.  Slots are
-//    claimed with a per-call epoch: a CTA whose SM slot is already taken takes any unclaimed slot,
-//    and the last CTA to finish processes slots nobody claimed, so every row is computed exactly
-//    once whatever the block scheduler does.  Nothing in the kernel waits on another CTA.
-//  * The granule-ring kernels (batch 1, rows on 4 KiB granules; the default wherever they apply)
-//    stream A into shared memory with TMA bulk copies and replace the slots by row pools that warps
-//    claim a chunk at a time, so SMs that get less bandwidth take fewer rows.  A split row's two
-//    partials meet in one 64-bit exchange word per row (see walk_pools).
+//  * (Register kernels.)  Rows are blocked per slot (one slot per SM) and interleaved over the CTA's
+//    warps.  Slots are claimed with a per-call epoch: a CTA whose SM slot is already taken takes
+//    any unclaimed slot, and the last CTA to finish processes slots nobody claimed, so every row is
+//    computed exactly once whatever the block scheduler does.  Nothing in the kernel waits on
+//    another CTA.
+//  * The granule-ring kernels (rows on 4 KiB granules, one problem or a batch; the default wherever
+//    they apply) stream A into shared memory with TMA bulk copies and replace the slots by row
+//    pools that warps claim a chunk at a time, so SMs that get less bandwidth take fewer rows.  A
+//    split row's two partials, and a tail row's two halves, meet in one 64-bit exchange word per
+//    row (see walk_pools).  A CTA whose SM slot is taken takes over a free slot at once (ring_call),
+//    so no CTA counts or waits for the others and a launch ends with its last walk.
+//  * The split modes place A by granule (near-only reads) or by whole row (the reference's rule);
+//    the plan picks by row length (auto_placement).
 #include "l2d_device.cuh"
 #include "l2d_internal.h"
 
